@@ -1,0 +1,312 @@
+// gemm_sm100.cuh — persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+// What it replaces in the reference (hustc12/hexagon-mlir):
+//   * the VTCM tile scheduler (lib/Conversion/LinalgToLLVM/VTCMTiling.cpp:231-266,
+//     VTCMTilingOptions.cpp:374-432): tiles are 128 x BN x (128 bytes of K),
+//     sized to the 227 KB of shared memory instead of the 2 MB VTCM;
+//   * the DDR->VTCM DMA prefetch + double buffering
+//     (HexmemCpyToDMA.cpp:50-80, DoubleBufferGenericS1.cpp:10-19,
+//     UserDMA.cc:27,94,167): a STAGES-deep ring of TMA box loads completing
+//     on mbarriers, issued by one producer warp;
+//   * the HVX/HMX inner loop (TilingPass.cpp:108-292,
+//     DecomposeHexKLMatmulPass.cpp:148-222): tcgen05.mma 128xBNx(32 bytes)
+//     issued by one thread, accumulating in TMEM;
+//   * the 4-thread scf.forall split (FormVirtualThreadsPass.cpp:51-202):
+//     a persistent grid of one CTA per SM walking a grouped tile order;
+//   * the unfused epilogue generic (FusionPass.cpp:163,176-179): applied to
+//     the accumulator in registers by four epilogue warps.
+//
+// Warp roles (192 threads):
+//   warp 0      TMA producer (lane 0 issues)
+//   warp 1      TMEM allocator + UMMA issuer (lane 0 issues)
+//   warps 2..5  epilogue: TMEM -> registers -> fused epilogue -> global
+// TMEM holds two BN-column fp32/s32 accumulators so the epilogue of tile i
+// overlaps the mainloop of tile i+1.
+#pragma once
+#include <cuda.h>
+#include <stdint.h>
+
+#include "epilogue.cuh"
+#include "ptx.cuh"
+
+namespace hx {
+
+constexpr int kBM = 128;          // UMMA M (rows of A per tile)
+constexpr int kKBytes = 128;      // K bytes per stage (one 128B swizzle row)
+constexpr int kUmmaKBytes = 32;   // K bytes per UMMA instruction
+constexpr int kThreads = 192;
+
+struct GemmParams {
+  int32_t M, K;                   // rows of A/C, reduction length
+  int32_t n_tiles, m_tiles, k_blocks;
+  int32_t n_half;                 // SWIGLU: first row of the "up" half of B
+  int32_t group_m;                // grouped raster: m-tiles per group
+  int32_t total_tiles;
+  int32_t stages;                 // depth of the smem ring
+  uint64_t timeout;               // cycles per bounded wait
+  int32_t *err_flag;              // optional global error word
+  EpiArgs epi;
+};
+
+template <int BN, int KIND, bool B_MN, bool SWIGLU>
+struct GemmCfg {
+  static constexpr int kElem = (KIND == 2) ? 1 : 2;
+  static constexpr int kBKElems = kKBytes / kElem;               // 64 or 128
+  static constexpr int kUmmaK = kUmmaKBytes / kElem;              // 16 or 32
+  static constexpr int kABytes = kBM * kKBytes;                   // 16 KB
+  static constexpr int kBBytes = BN * kKBytes;                    // BN * 128 B
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBNOut = SWIGLU ? BN / 2 : BN;             // output columns / tile
+  static constexpr int kTmemCols = 2 * BN;                        // double-buffered acc
+  static constexpr int kMNChunk = kKBytes / kElem;                // MN elems per 128 B
+  static constexpr int smem_bytes(int stages) { return stages * kStageBytes + 1024 /*align*/ + 256 /*bars*/; }
+  static constexpr uint32_t kIdesc = make_idesc(KIND, B_MN, kBM, BN);
+  static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+  static_assert(!(SWIGLU && B_MN), "SWIGLU needs the W[N,K] layout");
+  static_assert(kTmemCols >= 32 && kTmemCols <= 512, "TMEM columns");
+};
+
+__device__ __forceinline__ void tile_coords(int t, const GemmParams &p, int &m_blk, int &n_blk) {
+  const int per_group = p.group_m * p.n_tiles;
+  const int g = t / per_group;
+  const int first_m = g * p.group_m;
+  const int gsize = min(p.m_tiles - first_m, p.group_m);
+  const int r = t - g * per_group;
+  m_blk = first_m + r % gsize;
+  n_blk = r / gsize;
+}
+
+__device__ __forceinline__ void raise_abort(volatile int *abort_flag, int32_t *err, int code) {
+  *abort_flag = 1;
+  if (err != nullptr) atomicExch(err, code);
+}
+
+template <int BN, int KIND, bool B_MN, bool SWIGLU>
+__global__ void __launch_bounds__(kThreads, 1)
+    hx_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
+                         const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ GemmParams p) {
+  using Cfg = GemmCfg<BN, KIND, B_MN, SWIGLU>;
+  const int STAGES = p.stages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the 128B-swizzle atoms.
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *sA = smem;
+  uint8_t *sB = smem + STAGES * Cfg::kABytes;
+  uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + STAGES * Cfg::kStageBytes);
+  uint64_t *empty_bar = full_bar + STAGES;
+  uint64_t *tfull_bar = empty_bar + STAGES;   // [2]
+  uint64_t *tempty_bar = tfull_bar + 2;       // [2]
+  uint64_t *drain_bar = tempty_bar + 2;       // [1]
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain_bar + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    int64_t issued = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+      int m_blk, n_blk;
+      tile_coords(t, p, m_blk, n_blk);
+      const int m0 = m_blk * kBM;
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        bool w = (lane == 0) ? mbar_wait(&empty_bar[stage], phase ^ 1, p.timeout, abort_flag)
+                             : true;
+        w = __shfl_sync(0xffffffffu, w, 0);
+        if (!w) {
+          if (lane == 0) raise_abort(abort_flag, p.err_flag, 1);
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          uint64_t *fb = &full_bar[stage];
+          mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
+          const int kx = kb * Cfg::kBKElems;
+          tma_load_2d(sA + stage * Cfg::kABytes, &tmA, fb, kx, m0);
+          uint8_t *dstB = sB + stage * Cfg::kBBytes;
+          if constexpr (B_MN) {
+            const int n0 = n_blk * BN;
+#pragma unroll
+            for (int j = 0; j < BN / Cfg::kMNChunk; ++j)
+              tma_load_2d(dstB + j * (Cfg::kBKElems * 128), &tmB, fb, n0 + j * Cfg::kMNChunk, kx);
+          } else if constexpr (SWIGLU) {
+            const int n0 = n_blk * (BN / 2);
+            tma_load_2d(dstB, &tmB, fb, kx, n0);
+            tma_load_2d(dstB + (BN / 2) * kKBytes, &tmB, fb, kx, p.n_half + n0);
+          } else {
+            tma_load_2d(dstB, &tmB, fb, kx, n_blk * BN);
+          }
+        }
+        __syncwarp();
+        ++issued;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    if (!ok && lane == 0) {
+      // Drain: every load still in flight lands before the CTA exits.
+      const int64_t first = issued > STAGES ? issued - STAGES : 0;
+      for (int64_t i = first; i < issued; ++i) {
+        int dummy_abort = 0;
+        mbar_wait(&full_bar[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1), p.timeout,
+                  &dummy_abort);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ UMMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    int it = 0;
+    bool ok = true;
+    bool any_mma = false;
+    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      bool w = (lane == 0) ? mbar_wait(&tempty_bar[acc], acc_phase ^ 1, p.timeout, abort_flag)
+                           : true;
+      w = __shfl_sync(0xffffffffu, w, 0);
+      if (!w) {
+        if (lane == 0) raise_abort(abort_flag, p.err_flag, 2);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        bool f = (lane == 0) ? mbar_wait(&full_bar[stage], phase, p.timeout, abort_flag) : true;
+        f = __shfl_sync(0xffffffffu, f, 0);
+        if (!f) {
+          if (lane == 0) raise_abort(abort_flag, p.err_flag, 3);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_base = smem_u32(sA + stage * Cfg::kABytes);
+          const uint32_t b_base = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kKBytes / kUmmaKBytes; ++k) {
+            const uint64_t adesc = sdesc_kmajor_sw128(a_base + k * kUmmaKBytes);
+            uint64_t bdesc;
+            if constexpr (B_MN) {
+              // UMMA K step = kUmmaK rows of K = kUmmaK/8 swizzle atoms of 1024 B.
+              bdesc = sdesc_mnmajor_sw128(b_base + k * (Cfg::kUmmaK / 8) * 1024,
+                                          Cfg::kBKElems * 128);
+            } else {
+              bdesc = sdesc_kmajor_sw128(b_base + k * kUmmaKBytes);
+            }
+            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+            if constexpr (KIND == 2)
+              umma_i8(d_tmem, adesc, bdesc, Cfg::kIdesc, accum);
+            else
+              umma_f16(d_tmem, adesc, bdesc, Cfg::kIdesc, accum);
+          }
+          umma_commit(&empty_bar[stage]);  // frees the smem stage when read
+          any_mma = true;
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&tfull_bar[acc]);  // accumulator ready
+      __syncwarp();
+    }
+    if (!ok && lane == 0 && any_mma) {
+      // Drain: wait until every issued UMMA has finished before TMEM is freed.
+      umma_commit(drain_bar);
+      int dummy_abort = 0;
+      mbar_wait(drain_bar, 0, p.timeout, &dummy_abort);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;                   // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+      int m_blk, n_blk;
+      tile_coords(t, p, m_blk, n_blk);
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      bool w = (lane == 0) ? mbar_wait(&tfull_bar[acc], acc_phase, p.timeout, abort_flag) : true;
+      w = __shfl_sync(0xffffffffu, w, 0);
+      if (!w) {
+        if (lane == 0) raise_abort(abort_flag, p.err_flag, 4);
+        break;
+      }
+      tc_fence_after();
+      const int m = m_blk * kBM + row_in_tile;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < Cfg::kBNOut / 32; ++c) {
+        uint32_t r[32];
+        uint32_t r2[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        if constexpr (SWIGLU) tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, r2);
+        tmem_ld_wait();
+        float v[32], up[32];
+        const int n0 = n_blk * Cfg::kBNOut + c * 32;
+        const bool raw_int = (KIND == 2) && (p.epi.c_dtype == HX_S32) && (p.epi.epi == HX_EPI_NONE);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if constexpr (KIND == 2)
+            v[j] = static_cast<float>(static_cast<int32_t>(r[j]));
+          else
+            v[j] = __uint_as_float(r[j]);
+          if constexpr (SWIGLU)
+            up[j] = __uint_as_float(r2[j]);
+          else
+            up[j] = 0.f;
+        }
+        if (!raw_int) epi_transform32(p.epi, v, up, m, n0);
+        epi_store32(p.epi, v, r, raw_int, m, n0);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+}
+
+}  // namespace hx

@@ -1,0 +1,636 @@
+// hx_gemm.cu — host side of the C ABI declared in include/hx_gemm.h.
+//
+// Validation, tile selection (the analogue of the reference's
+// VTCMTilingOptions::determineTileSizes, lib/Conversion/LinalgToLLVM/
+// VTCMTilingOptions.cpp:374-432, re-targeted from a 2 MB VTCM budget to
+// 227 KB of shared memory and 512 TMEM columns per SM), TMA descriptor
+// encoding and kernel launch.  Every entry returns a status code; nothing
+// aborts, and nothing is allocated per call.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "gemm_simt.cuh"
+#include "gemm_sm100.cuh"
+#include "gemv_w8a16.cuh"
+#include "hx_gemm.h"
+
+#define HX_VERSION 1
+
+namespace hx {
+namespace {
+
+thread_local std::string g_last_error;
+
+int cuda_fail(cudaError_t e, const char *where) {
+  g_last_error = std::string(where) + ": " + cudaGetErrorString(e);
+  return HX_E_CUDA;
+}
+int arg_fail(const char *why) {
+  g_last_error = why;
+  return HX_E_INVALID_ARG;
+}
+int unsupported(const char *why) {
+  g_last_error = why;
+  return HX_E_UNSUPPORTED;
+}
+
+// ------------------------------------------------------------ device cache
+struct DeviceInfo {
+  std::atomic<int> sms{0};
+  std::atomic<int> major{0};
+};
+DeviceInfo g_dev[64];
+
+int current_device_info(int *sms, int *major) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return arg_fail("device index out of range");
+  int s = g_dev[dev].sms.load(std::memory_order_acquire);
+  if (s == 0) {
+    int v = 0, mj = 0;
+    e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SMs)");
+    e = cudaDeviceGetAttribute(&mj, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(cc)");
+    g_dev[dev].major.store(mj, std::memory_order_relaxed);
+    g_dev[dev].sms.store(v, std::memory_order_release);
+    s = v;
+  }
+  *sms = s;
+  *major = g_dev[dev].major.load(std::memory_order_relaxed);
+  return HX_OK;
+}
+
+// ------------------------------------------------------------ TMA encode
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  std::call_once(g_encode_once, [] {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode;
+}
+
+// 2-D row-major tensor: `inner` contiguous elements per row, `outer` rows.
+int make_tmap(CUtensorMap *map, const void *ptr, int dtype, uint64_t inner, uint64_t outer,
+              uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+  auto enc = get_encode();
+  if (!enc) {
+    g_last_error = "cuTensorMapEncodeTiled unavailable";
+    return HX_E_CUDA;
+  }
+  CUtensorMapDataType dt;
+  uint64_t esz;
+  switch (dtype) {
+    case HX_F16: dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16; esz = 2; break;
+    case HX_BF16: dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; esz = 2; break;
+    case HX_S8: dt = CU_TENSOR_MAP_DATA_TYPE_UINT8; esz = 1; break;
+    default: return unsupported("tensor map dtype");
+  }
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * esz};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    g_last_error = "cuTensorMapEncodeTiled failed (code " + std::to_string(int(r)) + ")";
+    return HX_E_UNSUPPORTED;
+  }
+  return HX_OK;
+}
+
+int esize(int dtype) {
+  switch (dtype) {
+    case HX_F16:
+    case HX_BF16: return 2;
+    case HX_S8: return 1;
+    case HX_S32:
+    case HX_F32: return 4;
+    default: return 0;
+  }
+}
+__host__ __device__ inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in limit per block on sm_100
+constexpr uint64_t kDefaultTimeout = 4000000000ull;  // ~2 s at 2 GHz
+
+// ------------------------------------------------------------ launch
+template <int BN, int KIND, bool BMN, bool SW>
+int launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p, int grid,
+              cudaStream_t s) {
+  using Cfg = GemmCfg<BN, KIND, BMN, SW>;
+  auto kern = hx_gemm_sm100_kernel<BN, KIND, BMN, SW>;
+  const int smem = Cfg::smem_bytes(p.stages);
+  static std::atomic<int> configured{0};
+  if (configured.load(std::memory_order_acquire) < smem) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kMaxDynSmem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    configured.store(kMaxDynSmem, std::memory_order_release);
+  }
+  kern<<<grid, kThreads, smem, s>>>(ta, tb, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "hx_gemm_sm100_kernel launch");
+  return HX_OK;
+}
+
+template <int KIND, bool BMN, bool SW>
+int dispatch_bn(int bn, const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
+                int grid, cudaStream_t s) {
+  switch (bn) {
+    case 64:
+      if constexpr (!(BMN && KIND == 2)) return launch_tc<64, KIND, BMN, SW>(ta, tb, p, grid, s);
+      return unsupported("tile_n 64 with int8 B[K,N]");
+    case 128: return launch_tc<128, KIND, BMN, SW>(ta, tb, p, grid, s);
+    case 256: return launch_tc<256, KIND, BMN, SW>(ta, tb, p, grid, s);
+    default: return unsupported("tile_n");
+  }
+}
+
+template <int KIND>
+int dispatch_kind(int bn, bool bmn, bool sw, const CUtensorMap &ta, const CUtensorMap &tb,
+                  const GemmParams &p, int grid, cudaStream_t s) {
+  if (bmn) return dispatch_bn<KIND, true, false>(bn, ta, tb, p, grid, s);
+  if (sw) {
+    if constexpr (KIND == 2) return unsupported("SWIGLU with int8 inputs");
+    else return dispatch_bn<KIND, false, true>(bn, ta, tb, p, grid, s);
+  }
+  return dispatch_bn<KIND, false, false>(bn, ta, tb, p, grid, s);
+}
+
+int stage_bytes(int bn) { return kBM * kKBytes + bn * kKBytes; }
+
+// Tile width choice: fewest waves x per-tile cost over the SMs, largest BN
+// on ties (a wider tile reuses each A tile over more columns).
+int choose_bn(int64_t M, int64_t n_out, bool swiglu, bool int8_kn, int sms) {
+  const int64_t m_tiles = (M + kBM - 1) / kBM;
+  int best = 256;
+  int64_t best_cost = INT64_MAX;
+  for (int bn : {256, 128, 64}) {
+    if (int8_kn && bn < 128) continue;
+    const int out_w = swiglu ? bn / 2 : bn;
+    const int64_t tiles = m_tiles * ((n_out + out_w - 1) / out_w);
+    const int64_t waves = (tiles + sms - 1) / sms;
+    const int64_t cost = waves * (out_w + 64);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+int validate(const hx_gemm_desc *d) {
+  if (!d) return arg_fail("null descriptor");
+  if (d->M < 0 || d->N < 0 || d->K < 0) return arg_fail("negative size");
+  if (d->M > INT32_MAX || d->N > INT32_MAX / 2 || d->K > INT32_MAX)
+    return unsupported("size beyond int32 range");
+  if (d->a_dtype != d->b_dtype) return unsupported("A and B dtypes differ");
+  if (d->a_dtype != HX_F16 && d->a_dtype != HX_BF16 && d->a_dtype != HX_S8)
+    return unsupported("A/B dtype");
+  const bool is_int = d->a_dtype == HX_S8;
+  switch (d->c_dtype) {
+    case HX_F16:
+    case HX_BF16:
+    case HX_F32: break;
+    case HX_S32:
+      if (!is_int || d->epilogue != HX_EPI_NONE)
+        return unsupported("int32 output needs int8 inputs and no epilogue");
+      break;
+    default: return unsupported("C dtype");
+  }
+  if (d->b_layout != HX_B_NK && d->b_layout != HX_B_KN) return arg_fail("b_layout");
+  if (d->M == 0 || d->N == 0) return HX_OK;
+  if (!d->C || (d->K > 0 && (!d->A || !d->B))) return arg_fail("null A/B/C");
+  if (d->lda < std::max<int64_t>(d->K, 1)) return arg_fail("lda < K");
+  if (d->b_layout == HX_B_NK && d->ldb < std::max<int64_t>(d->K, 1)) return arg_fail("ldb < K");
+  if (d->b_layout == HX_B_KN && d->ldb < d->N) return arg_fail("ldb < N");
+  if (d->ldc < d->N) return arg_fail("ldc < N");
+  switch (d->epilogue) {
+    case HX_EPI_NONE: break;
+    case HX_EPI_BIAS:
+    case HX_EPI_BIAS_GELU_TANH:
+    case HX_EPI_BIAS_SILU:
+      if (!d->bias) return arg_fail("epilogue needs bias");
+      break;
+    case HX_EPI_BIAS_RESIDUAL:
+      if (!d->bias || !d->residual) return arg_fail("epilogue needs bias and residual");
+      if (d->ldr < d->N) return arg_fail("ldr < N");
+      break;
+    case HX_EPI_RESIDUAL:
+      if (!d->residual) return arg_fail("epilogue needs residual");
+      if (d->ldr < d->N) return arg_fail("ldr < N");
+      break;
+    case HX_EPI_SWIGLU:
+      if (d->b_layout != HX_B_NK) return unsupported("SWIGLU needs the W[N,K] layout");
+      if (is_int) return unsupported("SWIGLU with int8 inputs");
+      break;
+    case HX_EPI_DEQUANT_SCALE:
+      if (!d->scale) return arg_fail("epilogue needs scale");
+      break;
+    default: return arg_fail("epilogue");
+  }
+  if (d->bias && esize(d->bias_dtype) == 0) return arg_fail("bias dtype");
+  if (d->bias && d->bias_dtype == HX_S8) return arg_fail("bias dtype");
+  if (d->scale && (esize(d->scale_dtype) == 0 || d->scale_dtype == HX_S8))
+    return arg_fail("scale dtype");
+  if (d->residual && d->residual == d->C && d->ldr != d->ldc)
+    return arg_fail("in-place residual needs ldr == ldc");
+  return HX_OK;
+}
+
+EpiArgs make_epi(const hx_gemm_desc *d) {
+  EpiArgs e;
+  e.C = d->C;
+  e.ldc = d->ldc;
+  e.bias = d->bias;
+  e.residual = d->residual;
+  e.ldr = d->ldr;
+  e.scale = d->scale;
+  e.c_dtype = d->c_dtype;
+  e.bias_dtype = d->bias_dtype;
+  e.scale_dtype = d->scale_dtype;
+  e.epi = d->epilogue;
+  e.M = static_cast<int32_t>(d->M);
+  e.N = static_cast<int32_t>(d->N);
+  const int cz = esize(d->c_dtype);
+  e.c_vec_ok = aligned16(d->C) && ((d->ldc * cz) % 16 == 0);
+  e.r_vec_ok = d->residual && aligned16(d->residual) && ((d->ldr * cz) % 16 == 0);
+  return e;
+}
+
+int run_simt(const hx_gemm_desc *d, cudaStream_t s) {
+  SimtParams p;
+  p.M = static_cast<int32_t>(d->M);
+  p.N = static_cast<int32_t>(d->N);
+  p.K = static_cast<int32_t>(d->K);
+  p.A = d->A;
+  p.lda = d->lda;
+  p.B = d->B;
+  p.ldb = d->ldb;
+  p.ab_dtype = d->a_dtype;
+  p.b_kn = d->b_layout == HX_B_KN;
+  p.n_half = static_cast<int32_t>(d->N);
+  p.epi = make_epi(d);
+  dim3 grid((p.N + kSimtTile - 1) / kSimtTile, (p.M + kSimtTile - 1) / kSimtTile);
+  if (grid.y > 65535) return unsupported("M too large for the CUDA-core kernel");
+  const bool sw = d->epilogue == HX_EPI_SWIGLU;
+  if (d->a_dtype == HX_S8) {
+    hx_gemm_simt_kernel<int, false><<<grid, 256, 0, s>>>(p);
+  } else if (sw) {
+    hx_gemm_simt_kernel<float, true><<<grid, 256, 0, s>>>(p);
+  } else {
+    hx_gemm_simt_kernel<float, false><<<grid, 256, 0, s>>>(p);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "hx_gemm_simt_kernel launch");
+  return HX_OK;
+}
+
+int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
+  int rc = validate(d);
+  if (rc != HX_OK) return rc;
+  if (d->M == 0 || d->N == 0) return HX_OK;
+  int sms = 0, major = 0;
+  rc = current_device_info(&sms, &major);
+  if (rc != HX_OK) return rc;
+  if (major != 10) {
+    g_last_error = "current device is not sm_100";
+    return HX_E_NO_DEVICE;
+  }
+  const int ez = esize(d->a_dtype);
+  const bool swiglu = d->epilogue == HX_EPI_SWIGLU;
+  const bool bmn = d->b_layout == HX_B_KN;
+  const bool tma_ok = !d->force_simt && d->K > 0 && aligned16(d->A) && aligned16(d->B) &&
+                      (d->lda * ez) % 16 == 0 && (d->ldb * ez) % 16 == 0;
+  if (!tma_ok) return run_simt(d, s);
+
+  int bn = d->tile_n;
+  if (bn == 0) bn = choose_bn(d->M, d->N, swiglu, bmn && ez == 1, sms);
+  if (bn != 64 && bn != 128 && bn != 256) return arg_fail("tile_n must be 64, 128 or 256");
+  if (bmn && ez == 1 && bn < 128) return unsupported("tile_n 64 with int8 B[K,N]");
+  int stages = d->stages;
+  const int max_stages = std::min(8, (kMaxDynSmem - 1280) / stage_bytes(bn));
+  if (stages == 0) stages = max_stages;
+  if (stages < 2 || stages > max_stages) return arg_fail("stages out of range for tile_n");
+
+  const int kind = d->a_dtype == HX_F16 ? 0 : (d->a_dtype == HX_BF16 ? 1 : 2);
+  const int bk = kKBytes / ez;
+  const int out_w = swiglu ? bn / 2 : bn;
+
+  CUtensorMap ta, tb;
+  rc = make_tmap(&ta, d->A, d->a_dtype, d->K, d->M, d->lda, bk, kBM);
+  if (rc != HX_OK) return rc;
+  if (bmn) {
+    rc = make_tmap(&tb, d->B, d->b_dtype, d->N, d->K, d->ldb, kKBytes / ez, bk);
+  } else {
+    const uint64_t rows = swiglu ? 2 * d->N : d->N;
+    rc = make_tmap(&tb, d->B, d->b_dtype, d->K, rows, d->ldb, bk, swiglu ? bn / 2 : bn);
+  }
+  if (rc != HX_OK) return rc;
+
+  GemmParams p;
+  p.M = static_cast<int32_t>(d->M);
+  p.K = static_cast<int32_t>(d->K);
+  p.m_tiles = static_cast<int32_t>((d->M + kBM - 1) / kBM);
+  p.n_tiles = static_cast<int32_t>((d->N + out_w - 1) / out_w);
+  p.k_blocks = static_cast<int32_t>((d->K + bk - 1) / bk);
+  p.n_half = static_cast<int32_t>(d->N);
+  p.group_m = std::min<int32_t>(16, p.m_tiles);
+  const int64_t total = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
+  if (total > INT32_MAX) return unsupported("too many tiles");
+  p.total_tiles = static_cast<int32_t>(total);
+  p.stages = stages;
+  p.timeout = d->timeout_cycles ? d->timeout_cycles : kDefaultTimeout;
+  p.err_flag = d->error_flag;
+  p.epi = make_epi(d);
+
+  int ctas = sms;
+  if (d->max_ctas > 0) ctas = std::min(ctas, static_cast<int>(d->max_ctas));
+  const int grid = static_cast<int>(std::min<int64_t>(total, ctas));
+
+  switch (kind) {
+    case 0: return dispatch_kind<0>(bn, bmn, swiglu, ta, tb, p, grid, s);
+    case 1: return dispatch_kind<1>(bn, bmn, swiglu, ta, tb, p, grid, s);
+    default: return dispatch_kind<2>(bn, bmn, swiglu, ta, tb, p, grid, s);
+  }
+}
+
+// ------------------------------------------------------------ W8A16
+int gemv_impl(int64_t M, int64_t N, int64_t K, const void *x, int64_t ldx, const int8_t *W,
+              int64_t ldw, const void *scale, const void *bias, void *y, int64_t ldy,
+              cudaStream_t s) {
+  if (M < 0 || N < 0 || K < 0) return arg_fail("negative size");
+  if (M == 0 || N == 0) return HX_OK;
+  if (!x || !W || !scale || !y) return arg_fail("null pointer");
+  if (ldx < K || ldw < K || ldy < N) return arg_fail("leading dimension too small");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return unsupported("size");
+  GemvParams p;
+  p.M = static_cast<int32_t>(M);
+  p.N = static_cast<int32_t>(N);
+  p.K = static_cast<int32_t>(K);
+  p.x = static_cast<const __half *>(x);
+  p.ldx = ldx;
+  p.W = W;
+  p.ldw = ldw;
+  p.scale = static_cast<const __half *>(scale);
+  p.bias = static_cast<const __half *>(bias);
+  p.y = static_cast<__half *>(y);
+  p.ldy = ldy;
+  const bool vec = K > 0 && K % 16 == 0 && ldw % 16 == 0 && ldx % 8 == 0 && aligned16(x) &&
+                   aligned16(W);
+  cudaError_t e;
+  if (vec) {
+    int mc = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
+    while (mc > 1 && static_cast<int64_t>(mc) * K * 2 > kMaxDynSmem) mc >>= 1;
+    const int64_t smem = static_cast<int64_t>(mc) * K * 2;
+    if (smem <= kMaxDynSmem) {
+      constexpr int ROWS = 2;
+      const int64_t blocks = (N + 4 * ROWS - 1) / (4 * ROWS);
+      auto launch = [&](auto kern) -> cudaError_t {
+        cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kMaxDynSmem);
+        if (r != cudaSuccess) return r;
+        kern<<<static_cast<unsigned>(blocks), 128, static_cast<size_t>(smem), s>>>(p);
+        return cudaGetLastError();
+      };
+      switch (mc) {
+        case 1: e = launch(hx_gemv_w8a16_kernel<ROWS, 1>); break;
+        case 2: e = launch(hx_gemv_w8a16_kernel<ROWS, 2>); break;
+        case 4: e = launch(hx_gemv_w8a16_kernel<ROWS, 4>); break;
+        default: e = launch(hx_gemv_w8a16_kernel<ROWS, 8>); break;
+      }
+      if (e != cudaSuccess) return cuda_fail(e, "hx_gemv_w8a16_kernel");
+      return HX_OK;
+    }
+  }
+  const int64_t warps = M * N;
+  const int64_t blocks = (warps * 32 + 127) / 128;
+  if (blocks > INT32_MAX) return unsupported("size");
+  hx_gemv_w8a16_scalar_kernel<<<static_cast<unsigned>(blocks), 128, 0, s>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "hx_gemv_w8a16_scalar_kernel");
+  return HX_OK;
+}
+
+// ------------------------------------------------------------ shard reorder
+// src[world][M][Ns] (rank-major all-gather result) -> dst[M][world*Ns].
+__global__ void shards_to_rows_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst,
+                                      int world, int64_t M, int64_t row_bytes) {
+  // one 16-byte (or 1-byte tail) chunk per thread, row-major over dst
+  const int64_t dst_row = row_bytes * world;
+  const int64_t chunks_per_row = (row_bytes + 15) / 16;
+  const int64_t total = M * world * chunks_per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t c = i % chunks_per_row;
+    const int64_t rm = i / chunks_per_row;
+    const int64_t r = rm % world, m = rm / world;
+    const uint8_t *sp = src + (r * M + m) * row_bytes + c * 16;
+    uint8_t *dp = dst + m * dst_row + r * row_bytes + c * 16;
+    const int64_t rem = row_bytes - c * 16;
+    const int64_t n = rem < 16 ? rem : 16;
+    if (n == 16 && aligned16(sp) && aligned16(dp)) {
+      *reinterpret_cast<uint4 *>(dp) = *reinterpret_cast<const uint4 *>(sp);
+    } else {
+      for (int64_t b = 0; b < n; ++b) dp[b] = sp[b];
+    }
+  }
+}
+
+}  // namespace
+}  // namespace hx
+
+// NCCL's ABI, restated for the dlopen'd symbols (nccl.h 2.x).
+typedef struct {
+  char internal[128];
+} hx_nccl_unique_id_t;
+typedef int (*hx_nccl_get_unique_id_fn)(hx_nccl_unique_id_t *);
+typedef int (*hx_nccl_comm_init_rank_fn)(void **, int, hx_nccl_unique_id_t, int);
+typedef int (*hx_nccl_all_gather_fn)(const void *, void *, size_t, int /*ncclDataType_t*/,
+                                     void * /*comm*/, cudaStream_t);
+typedef int (*hx_nccl_comm_destroy_fn)(void *);
+typedef const char *(*hx_nccl_error_string_fn)(int);
+
+namespace {
+struct NcclSyms {
+  hx_nccl_get_unique_id_fn get_unique_id = nullptr;
+  hx_nccl_comm_init_rank_fn comm_init_rank = nullptr;
+  hx_nccl_all_gather_fn all_gather = nullptr;
+  hx_nccl_comm_destroy_fn comm_destroy = nullptr;
+  hx_nccl_error_string_fn error_string = nullptr;
+};
+NcclSyms g_nccl;
+std::once_flag g_nccl_once;
+
+bool load_nccl() {
+  std::call_once(g_nccl_once, [] {
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    g_nccl.get_unique_id = reinterpret_cast<hx_nccl_get_unique_id_fn>(dlsym(h, "ncclGetUniqueId"));
+    g_nccl.comm_init_rank =
+        reinterpret_cast<hx_nccl_comm_init_rank_fn>(dlsym(h, "ncclCommInitRank"));
+    g_nccl.all_gather = reinterpret_cast<hx_nccl_all_gather_fn>(dlsym(h, "ncclAllGather"));
+    g_nccl.comm_destroy = reinterpret_cast<hx_nccl_comm_destroy_fn>(dlsym(h, "ncclCommDestroy"));
+    g_nccl.error_string = reinterpret_cast<hx_nccl_error_string_fn>(dlsym(h, "ncclGetErrorString"));
+  });
+  return g_nccl.get_unique_id && g_nccl.comm_init_rank && g_nccl.all_gather &&
+         g_nccl.comm_destroy;
+}
+int nccl_fail(int r, const char *where) {
+  hx::g_last_error = std::string(where) + ": " +
+                     (g_nccl.error_string ? g_nccl.error_string(r) : std::to_string(r));
+  return HX_E_NCCL;
+}
+}  // namespace
+
+// ============================================================ C ABI
+extern "C" {
+
+int hx_version(void) { return HX_VERSION; }
+
+const char *hx_status_str(int status) {
+  switch (status) {
+    case HX_OK: return "HX_OK";
+    case HX_E_INVALID_ARG: return "HX_E_INVALID_ARG";
+    case HX_E_UNSUPPORTED: return "HX_E_UNSUPPORTED";
+    case HX_E_CUDA: return "HX_E_CUDA";
+    case HX_E_TIMEOUT: return "HX_E_TIMEOUT";
+    case HX_E_NCCL: return "HX_E_NCCL";
+    case HX_E_NO_DEVICE: return "HX_E_NO_DEVICE";
+    case HX_E_TOO_LARGE: return "HX_E_TOO_LARGE";
+    default: return "HX_E_UNKNOWN";
+  }
+}
+
+const char *hx_last_error(void) { return hx::g_last_error.c_str(); }
+
+int hx_gemm(const hx_gemm_desc *d, void *stream) {
+  hx::g_last_error.clear();
+  return hx::gemm_impl(d, static_cast<cudaStream_t>(stream));
+}
+
+int hx_matmul_f16f16_f32(int64_t n_row, int64_t n_col, int64_t n_inner, float *out,
+                         const void *act, const void *W, void *stream) {
+  hx_gemm_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.M = n_row;
+  d.N = n_col;
+  d.K = n_inner;
+  d.a_dtype = d.b_dtype = HX_F16;
+  d.c_dtype = HX_F32;
+  d.b_layout = HX_B_KN;
+  d.A = act;
+  d.lda = n_inner;
+  d.B = W;
+  d.ldb = n_col;
+  d.C = out;
+  d.ldc = n_col;
+  d.epilogue = HX_EPI_NONE;
+  return hx_gemm(&d, stream);
+}
+
+int hx_gemv_w8a16(int64_t M, int64_t N, int64_t K, const void *x, int64_t ldx, const int8_t *W,
+                  int64_t ldw, const void *scale, const void *bias, void *y, int64_t ldy,
+                  void *stream) {
+  hx::g_last_error.clear();
+  return hx::gemv_impl(M, N, K, x, ldx, W, ldw, scale, bias, y, ldy,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int hx_query_workspace(const hx_gemm_desc *d, int64_t *bytes) {
+  if (!d || !bytes) return HX_E_INVALID_ARG;
+  *bytes = 0;
+  return HX_OK;
+}
+
+int hx_nccl_unique_id_size(void) { return static_cast<int>(sizeof(hx_nccl_unique_id_t)); }
+
+int hx_nccl_get_unique_id(void *id_out) {
+  if (!id_out) return HX_E_INVALID_ARG;
+  if (!load_nccl()) {
+    hx::g_last_error = "libnccl.so.2 not loadable";
+    return HX_E_NCCL;
+  }
+  hx_nccl_unique_id_t id;
+  int r = g_nccl.get_unique_id(&id);
+  if (r != 0) return nccl_fail(r, "ncclGetUniqueId");
+  std::memcpy(id_out, &id, sizeof(id));
+  return HX_OK;
+}
+
+int hx_nccl_comm_init(void **comm_out, int world, const void *id, int rank) {
+  if (!comm_out || !id || world < 1 || rank < 0 || rank >= world) return HX_E_INVALID_ARG;
+  if (!load_nccl()) {
+    hx::g_last_error = "libnccl.so.2 not loadable";
+    return HX_E_NCCL;
+  }
+  hx_nccl_unique_id_t uid;
+  std::memcpy(&uid, id, sizeof(uid));
+  int r = g_nccl.comm_init_rank(comm_out, world, uid, rank);
+  if (r != 0) return nccl_fail(r, "ncclCommInitRank");
+  return HX_OK;
+}
+
+int hx_nccl_comm_destroy(void *comm) {
+  if (!comm) return HX_E_INVALID_ARG;
+  if (!load_nccl()) return HX_E_NCCL;
+  int r = g_nccl.comm_destroy(comm);
+  if (r != 0) return nccl_fail(r, "ncclCommDestroy");
+  return HX_OK;
+}
+
+int hx_sharded_gemm_allgather(const hx_gemm_desc *d, int rank, int world, void *comm,
+                              void *gathered, void *stream) {
+  if (!d || world < 1 || rank < 0 || rank >= world) return HX_E_INVALID_ARG;
+  int rc = hx_gemm(d, stream);
+  if (rc != HX_OK || gathered == nullptr) return rc;
+  if (d->ldc != d->N) {
+    hx::g_last_error = "gather needs a contiguous shard (ldc == N)";
+    return HX_E_INVALID_ARG;
+  }
+  if (!comm) return HX_E_INVALID_ARG;
+  if (!load_nccl()) return HX_E_NCCL;
+  const size_t bytes = static_cast<size_t>(d->M) * d->N * hx::esize(d->c_dtype);
+  // ncclInt8 == 0: gather raw bytes.
+  int r = g_nccl.all_gather(d->C, gathered, bytes, 0, comm, static_cast<cudaStream_t>(stream));
+  if (r != 0) return nccl_fail(r, "ncclAllGather");
+  return HX_OK;
+}
+
+int hx_shards_to_rows(const void *src, void *dst, int world, int64_t M, int64_t shard_cols,
+                      int elem_bytes, void *stream) {
+  if (!src || !dst || world < 1 || M < 0 || shard_cols < 0 || elem_bytes <= 0)
+    return HX_E_INVALID_ARG;
+  const int64_t row_bytes = shard_cols * elem_bytes;
+  const int64_t total = M * world * ((row_bytes + 15) / 16);
+  if (total == 0) return HX_OK;
+  const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
+  hx::shards_to_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                              static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t *>(src), static_cast<uint8_t *>(dst), world, M, row_bytes);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return hx::cuda_fail(e, "shards_to_rows_kernel");
+  return HX_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,284 @@
+"""Torch-tensor front end of the B200 linear-layer kernels.
+
+Each function checks its tensors, fills the C descriptor and calls the
+library on the current CUDA stream.  The tensors must already be on an
+sm_100 GPU; nothing here computes on the CPU and nothing falls back to
+torch.matmul.
+
+Reference behaviour mirrored: a linear layer is `linalg.matmul` on
+`matmul_transpose_b` operands (W[N,K], folded by
+lib/Transforms/ScheduleMatmulForHVXPass.cpp:84-93) followed by an
+elementwise `linalg.generic` (bias, GELU-tanh, SiLU, residual add, cast;
+lowered separately in lib/Conversion/LinalgToLLVM/FusionPass.cpp:163-179).
+Here both run in one kernel.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+_DT = {
+    torch.float16: _lib.HX_F16,
+    torch.bfloat16: _lib.HX_BF16,
+    torch.int8: _lib.HX_S8,
+    torch.int32: _lib.HX_S32,
+    torch.float32: _lib.HX_F32,
+}
+
+
+def _dtype_code(t: torch.Tensor, what: str) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"{what}: unsupported dtype {t.dtype}") from None
+
+
+def _check_cuda(t: torch.Tensor, what: str, device: Optional[torch.device] = None) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{what} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{what} must be a CUDA tensor (there is no CPU path)")
+    if device is not None and t.device != device:
+        raise ValueError(f"{what} is on {t.device}, expected {device}")
+
+
+def _row_major_2d(t: torch.Tensor, what: str) -> int:
+    """Return the leading dimension of a 2-D tensor with unit column stride."""
+    if t.dim() != 2:
+        raise ValueError(f"{what} must be 2-D, got shape {tuple(t.shape)}")
+    if t.stride(1) != 1 and t.shape[1] > 1:
+        raise ValueError(f"{what} must have unit stride along its last dimension")
+    return max(t.stride(0), t.shape[1], 1)
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    *,
+    b_layout: str = "nk",
+    out: Optional[torch.Tensor] = None,
+    out_dtype: Optional[torch.dtype] = None,
+    epilogue: str = "none",
+    bias: Optional[torch.Tensor] = None,
+    residual: Optional[torch.Tensor] = None,
+    scale: Optional[torch.Tensor] = None,
+    tile_n: int = 0,
+    stages: int = 0,
+    max_ctas: int = 0,
+    force_simt: bool = False,
+    error_flag: Optional[torch.Tensor] = None,
+    timeout_cycles: int = 0,
+) -> torch.Tensor:
+    """out = epilogue(a @ B) with B = b.T (b_layout "nk", b is W[N,K]) or
+    B = b (b_layout "kn", b is [K,N]).
+
+    For epilogue "swiglu", b is the fused [gate; up] weight of 2N rows and
+    out = silu(a @ gate.T) * (a @ up.T) has N columns.
+    """
+    _check_cuda(a, "a")
+    dev = a.device
+    _check_cuda(b, "b", dev)
+    if epilogue not in _lib.EPILOGUES:
+        raise ValueError(f"unknown epilogue {epilogue!r}; one of {sorted(_lib.EPILOGUES)}")
+    epi = _lib.EPILOGUES[epilogue]
+    lda = _row_major_2d(a, "a")
+    ldb = _row_major_2d(b, "b")
+    M, K = a.shape
+    if b_layout == "nk":
+        nb, kb = b.shape
+        N = nb // 2 if epi == _lib.HX_EPI_SWIGLU else nb
+        if epi == _lib.HX_EPI_SWIGLU and nb % 2:
+            raise ValueError("swiglu weight must have an even number of rows")
+        layout = _lib.HX_B_NK
+    elif b_layout == "kn":
+        kb, N = b.shape
+        layout = _lib.HX_B_KN
+    else:
+        raise ValueError("b_layout must be 'nk' or 'kn'")
+    if kb != K:
+        raise ValueError(f"inner dimensions differ: a has K={K}, b has K={kb}")
+    if a.dtype != b.dtype:
+        raise TypeError(f"a and b dtypes differ ({a.dtype} vs {b.dtype})")
+    if out is None:
+        if out_dtype is None:
+            out_dtype = torch.int32 if (a.dtype == torch.int8 and epi == _lib.HX_EPI_NONE) else (
+                torch.float16 if a.dtype == torch.int8 else a.dtype)
+        out = torch.empty((M, N), dtype=out_dtype, device=dev)
+    else:
+        _check_cuda(out, "out", dev)
+        if tuple(out.shape) != (M, N):
+            raise ValueError(f"out has shape {tuple(out.shape)}, expected {(M, N)}")
+    ldc = _row_major_2d(out, "out")
+
+    d = _lib.HxGemmDesc()
+    d.M, d.N, d.K = M, N, K
+    d.a_dtype = d.b_dtype = _dtype_code(a, "a")
+    d.c_dtype = _dtype_code(out, "out")
+    d.b_layout = layout
+    d.A, d.lda = a.data_ptr(), lda
+    d.B, d.ldb = b.data_ptr(), ldb
+    d.C, d.ldc = out.data_ptr(), ldc
+    d.epilogue = epi
+    if bias is not None:
+        _check_cuda(bias, "bias", dev)
+        if bias.dim() != 1 or bias.shape[0] != N or bias.stride(0) != 1:
+            raise ValueError(f"bias must be a contiguous vector of {N}")
+        d.bias, d.bias_dtype = bias.data_ptr(), _dtype_code(bias, "bias")
+    if residual is not None:
+        _check_cuda(residual, "residual", dev)
+        if tuple(residual.shape) != (M, N) or residual.dtype != out.dtype:
+            raise ValueError("residual must match out in shape and dtype")
+        d.residual, d.ldr = residual.data_ptr(), _row_major_2d(residual, "residual")
+    if scale is not None:
+        _check_cuda(scale, "scale", dev)
+        if scale.dim() != 1 or scale.shape[0] != N or scale.stride(0) != 1:
+            raise ValueError(f"scale must be a contiguous vector of {N}")
+        d.scale, d.scale_dtype = scale.data_ptr(), _dtype_code(scale, "scale")
+    d.tile_n, d.stages, d.max_ctas = tile_n, stages, max_ctas
+    d.force_simt = 1 if force_simt else 0
+    if error_flag is not None:
+        _check_cuda(error_flag, "error_flag", dev)
+        if error_flag.dtype != torch.int32 or error_flag.numel() < 1:
+            raise ValueError("error_flag must be an int32 CUDA tensor")
+        d.error_flag = error_flag.data_ptr()
+    d.timeout_cycles = timeout_cycles
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.hx_gemm(ctypes.byref(d), ctypes.c_void_p(_stream_ptr(dev)))
+    _lib.check(rc, "hx_gemm")
+    return out
+
+
+def linear(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    bias: Optional[torch.Tensor] = None,
+    *,
+    activation: Optional[str] = None,
+    residual: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None,
+    **kw,
+) -> torch.Tensor:
+    """nn.Linear forward with a fused epilogue: act(x @ W.T + bias) + residual.
+
+    activation: None | "gelu_tanh" | "silu" | "swiglu" (weight = [gate; up]).
+    Leading dimensions of x are flattened, as aten.linear does.
+    """
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    r2 = residual.reshape(-1, residual.shape[-1]) if residual is not None else None
+    if activation is None:
+        if bias is not None and residual is not None:
+            epi = "bias_residual"
+        elif bias is not None:
+            epi = "bias"
+        elif residual is not None:
+            epi = "residual"
+        else:
+            epi = "none"
+    elif activation == "gelu_tanh":
+        if residual is not None or bias is None:
+            raise ValueError("gelu_tanh epilogue takes a bias and no residual")
+        epi = "bias_gelu_tanh"
+    elif activation == "silu":
+        if residual is not None or bias is None:
+            raise ValueError("silu epilogue takes a bias and no residual")
+        epi = "bias_silu"
+    elif activation == "swiglu":
+        if residual is not None or bias is not None:
+            raise ValueError("swiglu epilogue takes no bias or residual")
+        epi = "swiglu"
+    else:
+        raise ValueError(f"unknown activation {activation!r}")
+    o2 = out.reshape(-1, out.shape[-1]) if out is not None else None
+    y = gemm(x2, weight, b_layout="nk", out=o2, epilogue=epi, bias=bias, residual=r2, **kw)
+    return y.reshape(*lead, y.shape[-1])
+
+
+def matmul(a: torch.Tensor, b: torch.Tensor, *, out: Optional[torch.Tensor] = None,
+           out_dtype: Optional[torch.dtype] = None, **kw) -> torch.Tensor:
+    """C = A @ B with B stored [K, N] (plain linalg.matmul / tl.dot)."""
+    return gemm(a, b, b_layout="kn", out=out, out_dtype=out_dtype, **kw)
+
+
+def matmul_f16f16_f32(act: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """HexKL drop-in (hexkl_matmul_f16f16_f32, bin/runtime/src/HexKLAPI.cpp:15):
+    out[f32, n_row x n_col] = act[f16, n_row x n_inner] @ W[f16, n_inner x n_col]."""
+    _check_cuda(act, "act")
+    _check_cuda(w, "W", act.device)
+    if act.dtype != torch.float16 or w.dtype != torch.float16:
+        raise TypeError("hexkl matmul takes f16 operands")
+    if not (act.is_contiguous() and w.is_contiguous()):
+        raise ValueError("hexkl matmul takes contiguous operands")
+    n_row, n_inner = act.shape
+    k2, n_col = w.shape
+    if k2 != n_inner:
+        raise ValueError("inner dimensions differ")
+    if out is None:
+        out = torch.empty((n_row, n_col), dtype=torch.float32, device=act.device)
+    lib = _lib.load()
+    with torch.cuda.device(act.device):
+        rc = lib.hx_matmul_f16f16_f32(n_row, n_col, n_inner, out.data_ptr(), act.data_ptr(),
+                                      w.data_ptr(), ctypes.c_void_p(_stream_ptr(act.device)))
+    _lib.check(rc, "hx_matmul_f16f16_f32")
+    return out
+
+
+def gemv_w8a16(x: torch.Tensor, w_int8: torch.Tensor, scale: torch.Tensor,
+               bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y[M,N] = x[M,K] @ (w_int8[N,K] * scale[N,None]).T (+ bias), f16 in/out."""
+    _check_cuda(x, "x")
+    dev = x.device
+    _check_cuda(w_int8, "w_int8", dev)
+    _check_cuda(scale, "scale", dev)
+    if x.dtype != torch.float16 or w_int8.dtype != torch.int8 or scale.dtype != torch.float16:
+        raise TypeError("gemv_w8a16 takes f16 x, int8 weight, f16 scale")
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    M, K = x2.shape
+    N, K2 = w_int8.shape
+    if K2 != K:
+        raise ValueError("inner dimensions differ")
+    if scale.numel() != N or not scale.is_contiguous():
+        raise ValueError("scale must be a contiguous vector of N")
+    if bias is not None:
+        _check_cuda(bias, "bias", dev)
+        if bias.dtype != torch.float16 or bias.numel() != N or not bias.is_contiguous():
+            raise ValueError("bias must be a contiguous f16 vector of N")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, device=dev)
+    o2 = out.reshape(-1, N)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.hx_gemv_w8a16(
+            M, N, K, x2.data_ptr(), _row_major_2d(x2, "x"), w_int8.data_ptr(),
+            _row_major_2d(w_int8, "w_int8"), scale.data_ptr(),
+            bias.data_ptr() if bias is not None else None, o2.data_ptr(),
+            _row_major_2d(o2, "out"), ctypes.c_void_p(_stream_ptr(dev)))
+    _lib.check(rc, "hx_gemv_w8a16")
+    return out.reshape(*lead, N)
+
+
+def shards_to_rows(gathered: torch.Tensor, world: int) -> torch.Tensor:
+    """[world, M, Ns] rank-major all-gather result -> row-major [M, world*Ns]."""
+    _check_cuda(gathered, "gathered")
+    if gathered.dim() != 3 or gathered.shape[0] != world or not gathered.is_contiguous():
+        raise ValueError("gathered must be a contiguous [world, M, Ns] tensor")
+    _, M, ns = gathered.shape
+    out = torch.empty((M, world * ns), dtype=gathered.dtype, device=gathered.device)
+    lib = _lib.load()
+    with torch.cuda.device(gathered.device):
+        rc = lib.hx_shards_to_rows(gathered.data_ptr(), out.data_ptr(), world, M, ns,
+                                   gathered.element_size(),
+                                   ctypes.c_void_p(_stream_ptr(gathered.device)))
+    _lib.check(rc, "hx_shards_to_rows")
+    return out

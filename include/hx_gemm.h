@@ -1,0 +1,175 @@
+/*
+ * hx_gemm.h — C ABI of the B200 (sm_100a) linear-layer GEMM library.
+ *
+ * This is the native boundary that replaces the reference's kernel ABIs for
+ * the tiled linear-layer matmul (linalg.matmul + its elementwise
+ * linalg.generic epilogue):
+ *
+ *   - the HexKL library call
+ *       int hexkl_matmul_f16f16_f32(int64_t n_row, int64_t n_col,
+ *                                   int64_t n_inner, float *out,
+ *                                   const _Float16 *act, const _Float16 *W)
+ *     (qcom_hexagon_backend/bin/runtime/src/HexKLAPI.cpp:15-17,
+ *      include/HexKLAPI.h), replaced by hx_matmul_f16f16_f32();
+ *   - the MLIR memref-descriptor kernel ABI that the launcher wrappers call
+ *     (qcom_hexagon_backend/backend/triton_hexagon_launcher.py:158-168,
+ *      torch_mlir_hexagon_launcher.py:68-88), and the `library_call`
+ *     escape hatch `_mlir_ciface_<fn>`
+ *     (lib/Transforms/ReplaceWithLibraryCallsPass.cpp:85-141),
+ *     both replaced by the descriptor call hx_gemm().
+ *
+ * Conventions (all entry points):
+ *   - The caller owns every buffer.  Pointers are device pointers unless the
+ *     name says host.  Nothing is allocated per call; the library keeps only
+ *     a per-device cache of the SM count and the driver's tensor-map encoder.
+ *   - Calls are asynchronous and ordered on the given CUDA stream
+ *     (cudaStream_t passed as void*; NULL = legacy default stream).
+ *   - Return value: HX_OK (0) or a negative HX_E_* code.  No call aborts or
+ *     exits the process.  hx_status_str() names a code.
+ *   - Row-major everywhere: A[M,K] (lda), C[M,N] (ldc).  B is either the
+ *     nn.Linear weight layout W[N,K] (HX_B_NK, the "matmul_transpose_b" form
+ *     the reference folds transpose+matmul into,
+ *     lib/Transforms/ScheduleMatmulForHVXPass.cpp:84-93) or B[K,N] (HX_B_KN,
+ *     plain linalg.matmul / tl.dot).
+ */
+#ifndef HX_GEMM_H
+#define HX_GEMM_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define HX_OK 0
+#define HX_E_INVALID_ARG -1   /* null pointer, negative size, bad enum      */
+#define HX_E_UNSUPPORTED -2   /* dtype / layout / epilogue combination       */
+#define HX_E_CUDA -3          /* a CUDA runtime or driver call failed        */
+#define HX_E_TIMEOUT -4       /* a bounded device wait ran out (see below)   */
+#define HX_E_NCCL -5          /* an NCCL call failed                         */
+#define HX_E_NO_DEVICE -6     /* no sm_100 device is current                 */
+#define HX_E_TOO_LARGE -7     /* size beyond a documented fixed limit        */
+
+/* ---- element types ------------------------------------------------------ */
+#define HX_F16 0
+#define HX_BF16 1
+#define HX_S8 2
+#define HX_S32 3
+#define HX_F32 4
+
+/* ---- B operand layout --------------------------------------------------- */
+#define HX_B_NK 0 /* B stored as W[N,K] row-major (nn.Linear weight)          */
+#define HX_B_KN 1 /* B stored as B[K,N] row-major                            */
+
+/* ---- fused epilogues (the linalg.generic ops that follow the matmul) ---- */
+#define HX_EPI_NONE 0           /* C = acc                                     */
+#define HX_EPI_BIAS 1           /* C = acc + bias[n]                           */
+#define HX_EPI_BIAS_GELU_TANH 2 /* C = gelu_tanh(acc + bias[n])                */
+#define HX_EPI_BIAS_RESIDUAL 3  /* C = acc + bias[n] + R[m,n]                  */
+#define HX_EPI_RESIDUAL 4       /* C = acc + R[m,n]                            */
+#define HX_EPI_SWIGLU 5         /* C = silu(acc_gate) * acc_up; B holds 2N rows:
+                                   rows [0,N) gate, rows [N,2N) up (HX_B_NK)   */
+#define HX_EPI_DEQUANT_SCALE 6  /* C = acc * scale[n] (+ bias[n] if given)     */
+#define HX_EPI_BIAS_SILU 7      /* C = silu(acc + bias[n])                     */
+
+/* Problem descriptor for hx_gemm().  Zero-initialise and fill what applies. */
+typedef struct hx_gemm_desc {
+  int64_t M, N, K;         /* C is M x N; for HX_EPI_SWIGLU, B has 2N rows    */
+  int32_t a_dtype;         /* HX_F16 | HX_BF16 | HX_S8                        */
+  int32_t b_dtype;         /* must equal a_dtype                              */
+  int32_t c_dtype;         /* HX_F16 | HX_BF16 | HX_F32 | HX_S32 (S32 only
+                              with S8 inputs and HX_EPI_NONE: exact int32)   */
+  int32_t b_layout;        /* HX_B_NK | HX_B_KN                               */
+  const void *A;
+  int64_t lda;             /* elements                                        */
+  const void *B;
+  int64_t ldb;             /* elements                                        */
+  void *C;
+  int64_t ldc;             /* elements                                        */
+  int32_t epilogue;        /* HX_EPI_*                                        */
+  int32_t bias_dtype;      /* dtype of bias[N] (HX_F16 | HX_BF16 | HX_F32)    */
+  const void *bias;        /* [N] or NULL                                     */
+  const void *residual;    /* [M, N] of c_dtype, or NULL                      */
+  int64_t ldr;             /* residual leading dimension, elements            */
+  int32_t scale_dtype;     /* dtype of scale[N] (HX_F16 | HX_BF16 | HX_F32)   */
+  const void *scale;       /* [N] per-output-channel scale, or NULL           */
+  /* Tile override (0 = choose automatically), the analogue of the
+     reference's HexagonOptions.tileSizes (backend/hexagon_options.py:75).
+     tile_n in {64,128,256}; stages in [2,8]. */
+  int32_t tile_n;
+  int32_t stages;
+  int32_t max_ctas;        /* cap on persistent CTAs (0 = one per SM)         */
+  int32_t force_simt;      /* 1 = use the CUDA-core kernel (validation only)  */
+  int32_t *error_flag;     /* optional device int32; set non-zero by a kernel
+                              whose bounded wait ran out                      */
+  uint64_t timeout_cycles; /* bound for each device wait (0 = ~2 s default)   */
+} hx_gemm_desc;
+
+/* C = epilogue(A . B).  Replaces the linalg.matmul + linalg.generic pair the
+   reference compiles through LinalgToLLVMPass
+   (lib/Conversion/LinalgToLLVM/LinalgToLLVMPass.cpp:188-400) and runs as the
+   _mlir_ciface_<fn> entry of the generated .so. */
+int hx_gemm(const hx_gemm_desc *d, void *stream);
+
+/* HexKL drop-in: out[n_row, n_col] (f32) = act[n_row, n_inner] (f16) .
+   W[n_inner, n_col] (f16), fp32 accumulate.  Replaces
+   hexkl_matmul_f16f16_f32 (bin/runtime/src/HexKLAPI.cpp:15-17); unlike
+   HexKL the accumulator is not rounded to f16 before widening. */
+int hx_matmul_f16f16_f32(int64_t n_row, int64_t n_col, int64_t n_inner,
+                         float *out, const void *act, const void *W,
+                         void *stream);
+
+/* W8A16 skinny-M decode GEMM: y[M,N] (f16) = x[M,K] (f16) . (W[N,K] (s8) *
+   scale[N] (f16))^T (+ bias[N] f16 if non-NULL), fp32 accumulate.  The
+   reference has no int8 GEMM kernel: it lowers quantised ops to dequantise +
+   float matmul (lib/Conversion/LinalgToLLVM/LinalgToLLVMPass.cpp:203-209) and
+   reduces unit-M matvec to a dot (lib/Transforms/
+   ReduceContractionRankPass.cpp:38-47); this entry replaces that pair. */
+int hx_gemv_w8a16(int64_t M, int64_t N, int64_t K, const void *x, int64_t ldx,
+                  const int8_t *W, int64_t ldw, const void *scale,
+                  const void *bias, void *y, int64_t ldy, void *stream);
+
+/* Column-sharded GEMM followed by an all-gather of the output over NCCL.
+   Rank r holds its shard of the weight, B rows [r*Ns, (r+1)*Ns) (HX_B_NK),
+   with Ns = d->N, and computes C_r = epilogue(A . B_r^T) into d->C
+   ([M, Ns], ldc must equal Ns for the gather).  The gather then fills
+   gathered[world][M][Ns] (rank-major, c_dtype) on every rank;
+   hx_shards_to_rows() turns that into the row-major logits [M, world*Ns].
+   Pass gathered = NULL to keep the output vocab-parallel.  `comm` comes from
+   hx_nccl_comm_init.  The reference has no multi-device path; this is the
+   N-sharding the B200 build adds. */
+int hx_sharded_gemm_allgather(const hx_gemm_desc *d, int rank, int world,
+                              void *comm, void *gathered, void *stream);
+
+/* dst[M, world*Ns] = concat over r of src[r][M][Ns] along columns
+   (elem_bytes per element). */
+int hx_shards_to_rows(const void *src, void *dst, int world, int64_t M,
+                      int64_t shard_cols, int elem_bytes, void *stream);
+
+/* NCCL communicator plumbing for hx_sharded_gemm_allgather.  The unique id
+   is an opaque blob of hx_nccl_unique_id_size() bytes that rank 0 creates
+   and the host sends to every rank (e.g. through torch.distributed). */
+int hx_nccl_unique_id_size(void);
+int hx_nccl_get_unique_id(void *id_out);
+int hx_nccl_comm_init(void **comm_out, int world, const void *id, int rank);
+int hx_nccl_comm_destroy(void *comm);
+
+/* Scratch bytes a call with this descriptor needs from the caller (the
+   current kernels need none: returns 0 in *bytes). */
+int hx_query_workspace(const hx_gemm_desc *d, int64_t *bytes);
+
+/* Human-readable name of a status code. */
+const char *hx_status_str(int status);
+
+/* Last CUDA error text recorded by this thread's failing call, or "". */
+const char *hx_last_error(void);
+
+/* Library version, for the Python loader's sanity check. */
+int hx_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HX_GEMM_H */
