@@ -1,0 +1,494 @@
+"""Benchmark of the B200 linear-layer GEMM path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl hx|reference]
+                    [--workload gpt2|qwen|tinyllama|lmhead|cube]
+
+Default workload (the configuration the headline metric is quoted on): the
+GPT-2-small linear stack, fp16, batch 1 x seq 1024, hidden 768, 12 layers
+(QKV +bias, attn-out +bias+residual, MLP-up +bias+GELU-tanh, MLP-down
++bias+residual), random-init weights N(0,0.02), activations N(0,1).
+
+A "step" is one forward of the whole stack (48 fused GEMM launches,
+173.95 GFLOP), replayed from a CUDA graph.  Each timed step is bracketed by
+CUDA events on the launching stream with a 256 MB L2 flush before it
+(outside the events).  Multi-GPU: one process per GPU under torchrun; the
+GPT-2/Qwen stacks run as independent replicas (weak scaling), the LM head
+is column-sharded over N (strong scaling).  Time is the max over ranks.
+
+--impl reference runs the reference's own CPU path for the same workload
+(PyTorch-CPU F.linear + epilogue in the config dtype, the golden every
+reference test compares against) on rank 0 with all host threads.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "hexagon-mlir_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+from qcom_hexagon_backend import workloads as WL  # noqa: E402
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    except (OSError, ValueError):
+        return FALLBACK_PEAKS, "fallback"
+
+
+def read_traffic(name):
+    """Per-launch DRAM bytes recorded from an ncu capture (profiles/<name>), or None."""
+    p = os.path.join(ROOT, "profiles", name)
+    try:
+        with open(p) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi during the timed region (SM clock + throttle reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 5.0:  # first sample before the timed region
+            time.sleep(0.02)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- dist
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo")
+    if world != n_gpus and rank == 0:
+        print(f"warning: --gpus {n_gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world, dev):
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+    torch.cuda.synchronize(dev)
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_reference_time(workload, budget_s=15.0):
+    """Reference's CPU golden path, bounded sample.  Returns (value, unit, sample, cores)."""
+    from oracle import cpu_reference as CR
+
+    n = cpu_threads()
+    torch.set_num_threads(n)
+    return CR.time_workload(workload, budget_s=budget_s, threads=n)
+
+
+# ---------------------------------------------------------------- workloads
+def build_gpt2(dev, seed=1234):
+    from qcom_hexagon_backend.backend import HexagonOptions, TorchMLIRHexagonLauncher
+
+    model = WL.GPT2LinearStack().half()
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(1024, 768, generator=g).half()
+    launcher = TorchMLIRHexagonLauncher()
+    cg = launcher.compile_torch_mlir(model, [x], "gpt2_linear_stack",
+                                     HexagonOptions(device=dev.index))
+    flops = WL.gpt2_stack_flops()
+    return dict(launcher=launcher, model=model, cg=cg, x=x, flops=flops, launches=cg.n_hx_calls,
+                metric="GEMM+epilogue TFLOP/s", unit="TFLOP/s", dtype="fp16",
+                config={"workload": "gpt2-small linear stack (BASELINE config 2)", "model": "gpt2-small-linears",
+                        "layers": 12, "global_batch": 1, "seq_len": 1024, "hidden": 768,
+                        "gemms_per_step": cg.n_hx_calls, "flops_per_step": flops},
+                traffic_file="gemm_gpt2_stack.txt", func="gpt2_linear_stack")
+
+
+def build_qwen(dev, seed=1235):
+    from qcom_hexagon_backend.backend import HexagonOptions, TorchMLIRHexagonLauncher
+
+    model = WL.QwenLinearStack().to(torch.bfloat16)
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(2048, 896, generator=g).to(torch.bfloat16)
+    launcher = TorchMLIRHexagonLauncher()
+    cg = launcher.compile_torch_mlir(model, [x], "qwen_linear_stack", HexagonOptions(device=dev.index))
+    flops = WL.qwen_stack_flops()
+    return dict(launcher=launcher, model=model, cg=cg, x=x, flops=flops, launches=cg.n_hx_calls,
+                metric="GEMM+epilogue TFLOP/s", unit="TFLOP/s", dtype="bf16",
+                config={"workload": "qwen2.5-0.5b prefill linear stack (BASELINE config 3)",
+                        "model": "qwen2.5-0.5b-linears", "layers": 24, "global_batch": 1, "seq_len": 2048,
+                        "gemms_per_step": cg.n_hx_calls, "flops_per_step": flops},
+                traffic_file="gemm_qwen_stack.txt", func="qwen_linear_stack")
+
+
+def time_graph_steps(cg, steps, flush, dev):
+    """Per-step CUDA-event times (ms) of graph replays, L2 flushed before each."""
+    stream = torch.cuda.current_stream(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for s, e in evs:
+        flush.zero_()
+        s.record(stream)
+        cg.launch()
+        e.record(stream)
+    torch.cuda.synchronize(dev)
+    return [s.elapsed_time(e) for s, e in evs]
+
+
+def kernel_roofline(cg, flops_per_step, launches, dev, peaks, reps=5):
+    """Average per-launch duration of the GEMM kernel, measured with CUDA
+    events around each launch on its stream (eager replay of the rewritten
+    graph).  achieved = algorithmic FLOPs per launch / that duration."""
+    from qcom_hexagon_backend import ops
+
+    stream = torch.cuda.current_stream(dev)
+    times = []
+    orig = ops.gemm
+
+    def timed_gemm(*a, **k):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        out = orig(*a, **k)
+        e.record(stream)
+        times.append((s, e))
+        return out
+
+    ops.gemm = timed_gemm
+    try:
+        with torch.no_grad():
+            for _ in range(reps):
+                # Park the GPU on a spin kernel while the host enqueues the
+                # launches, so the events bracket device time only.
+                torch.cuda._sleep(100_000_000)
+                cg.gm(*cg.static_in)
+                torch.cuda.synchronize(dev)
+    finally:
+        ops.gemm = orig
+    torch.cuda.synchronize(dev)
+    durs = [s.elapsed_time(e) for s, e in times]
+    total_ms = sum(durs) / reps
+    per_launch_ms = total_ms / max(1, launches)
+    achieved = flops_per_step / (total_ms / 1e3) / 1e12
+    return achieved, per_launch_ms, total_ms
+
+
+def run_hx(args):
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    peaks, peak_src = load_peaks()
+    if args.workload in ("lmhead",):
+        return run_lmhead(args, world, rank, dev, peaks, peak_src)
+    if args.workload == "tinyllama":
+        return run_tinyllama(args, world, rank, dev, peaks, peak_src)
+    W = build_gpt2(dev) if args.workload == "gpt2" else build_qwen(dev)
+    cg = W["cg"]
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        flush.zero_()
+        cg.launch()
+    barrier(world, dev)
+    clk = ClockSampler(local)
+    clk.start()
+    barrier(world, dev)
+    step_ms = time_graph_steps(cg, args.steps, flush, dev)
+    barrier(world, dev)
+    clocks = clk.stop()
+    total_ms = max_over_ranks(sum(step_ms), world, dev)
+    ms_per_step = total_ms / args.steps
+    value = W["flops"] * world / (total_ms / args.steps / 1e3) / 1e12
+
+    # e2e: the reference-facing call with host buffers (pinned), H2D + graph + D2H
+    launcher = W["launcher"]
+    x_host = W["x"].pin_memory()
+    out_host = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in cg.static_out]
+    for _ in range(2):
+        launcher.run_torch_mlir(W["model"], [x_host], W["func"], outputs=out_host)
+    barrier(world, dev)
+    stream = torch.cuda.current_stream(dev)
+    e2e_ms = []
+    for _ in range(args.steps):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        launcher.run_torch_mlir(W["model"], [x_host], W["func"], outputs=out_host)
+        e.record(stream)
+        e.synchronize()
+        e2e_ms.append(s.elapsed_time(e))
+    e2e_total = max_over_ranks(sum(e2e_ms), world, dev)
+    e2e_value = W["flops"] * world / (e2e_total / args.steps / 1e3) / 1e12
+    h2d = x_host.numel() * x_host.element_size()
+    d2h = sum(o.numel() * o.element_size() for o in out_host)
+
+    achieved, per_launch_ms, kern_ms = kernel_roofline(cg, W["flops"], W["launches"], dev, peaks)
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    traffic = read_traffic(W["traffic_file"])
+
+    line = {
+        "metric": W["metric"], "value": round(value, 2), "unit": W["unit"], "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": W["dtype"],
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) random-init weights)",
+        "config": dict(W["config"], parallelism=f"replicas{world}",
+                       l2="flushed (256 MB write) before every timed step"),
+        "e2e": {"value": round(e2e_value, 2), "unit": W["unit"], "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "api": "TorchMLIRHexagonLauncher.run_torch_mlir (pinned host in/out)"},
+        "gpu_launches": W["launches"] * args.steps,
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "kernel": "hx_gemm_sm100_kernel", "per_launch_ms": round(per_launch_ms, 5),
+                     "peak_source": f"{peak_src} bf16_tflops (burst; fp16 dense peak equals bf16)"},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, unit, sample, cores = cpu_reference_time(args.workload, budget_s=args.cpu_budget)
+        line["cpu_baseline"] = {"value": v, "unit": unit, "cores": cores, "kind": "port", "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_tinyllama(args, world, rank, dev, peaks, peak_src):
+    """Config 4: W8A16 decode linears, 22 layers x 7 projections, M in {1,8,32,64}."""
+    from qcom_hexagon_backend import ops
+
+    layers = WL.make_tinyllama_w8a16()
+    dl = [{p: (l[p].weight.to(dev), l[p].scale.to(dev)) for p in l} for l in layers]
+    M = args.batch
+    g = torch.Generator().manual_seed(1237)
+    x = torch.randn(M, 2048, generator=g).half().to(dev)
+    xi = torch.randn(M, 5632, generator=g).half().to(dev)
+    outs = {p: torch.empty(M, WL.tinyllama_shapes()[p][0], dtype=torch.float16, device=dev)
+            for p in WL.TINYLLAMA_PROJ}
+
+    def step():
+        for l in dl:
+            for p in WL.TINYLLAMA_PROJ:
+                w, s = l[p]
+                ops.gemv_w8a16(xi if p == "down" else x, w, s, out=outs[p])
+
+    step()
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        graph.replay()
+    barrier(world, dev)
+    clk = ClockSampler(dev.index)
+    clk.start()
+    stream = torch.cuda.current_stream(dev)
+    evs = []
+    for _ in range(args.steps):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        graph.replay()
+        e.record(stream)
+        evs.append((s, e))
+    barrier(world, dev)
+    clocks = clk.stop()
+    total = max_over_ranks(sum(s.elapsed_time(e) for s, e in evs), world, dev)
+    ms = total / args.steps
+    nbytes = WL.tinyllama_decode_bytes(M)
+    gbs = nbytes / (ms / 1e3) / 1e9
+    peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    line = {"metric": "W8A16 decode HBM GB/s", "value": round(gbs * world, 1), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 x f16 (f32 acc)", "data": "synthetic",
+            "config": {"workload": f"tinyllama-1.1b decode linears W8A16 M={M} (BASELINE config 4)",
+                       "layers": 22, "M": M, "bytes_per_step": nbytes, "l2": "flushed before every step",
+                       "parallelism": f"replicas{world}"},
+            "gpu_launches": 22 * 7 * args.steps,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "traffic": None, "kernel": "hx_gemv_w8a16_kernel",
+                         "peak_source": f"{peak_src} hbm_gbs"},
+            "clocks": clocks}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_lmhead(args, world, rank, dev, peaks, peak_src):
+    """Config 5: LM head M=16384 x K=2048 x N=50304 bf16, column-sharded over the ranks."""
+    from qcom_hexagon_backend import ops
+
+    M, K, N = WL.LMHEAD_M, WL.LMHEAD_K, WL.LMHEAD_N
+    ns = (N + world - 1) // world
+    n0, n1 = rank * ns, min(N, (rank + 1) * ns)
+    g = torch.Generator().manual_seed(1238)
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
+    w_full = torch.randn(N, K, generator=g)
+    w = (w_full[n0:n1] * 0.02).to(torch.bfloat16).to(dev)
+    del w_full
+    out = torch.empty(M, n1 - n0, dtype=torch.bfloat16, device=dev)
+    for _ in range(args.warmup):
+        ops.gemm(a, w, out=out)
+    barrier(world, dev)
+    clk = ClockSampler(dev.index)
+    clk.start()
+    stream = torch.cuda.current_stream(dev)
+    evs = []
+    for _ in range(args.steps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        ops.gemm(a, w, out=out)
+        e.record(stream)
+        evs.append((s, e))
+    barrier(world, dev)
+    clocks = clk.stop()
+    local_ms = sum(s.elapsed_time(e) for s, e in evs)
+    total = max_over_ranks(local_ms, world, dev)
+    ms = total / args.steps
+    flops = 2.0 * M * N * K
+    tflops = flops / (ms / 1e3) / 1e12
+    my_tflops = 2.0 * M * (n1 - n0) * K / (local_ms / args.steps / 1e3) / 1e12
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    line = {"metric": "GEMM+epilogue TFLOP/s", "value": round(tflops, 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "LM head 16384x2048x50304 bf16, column-sharded (BASELINE config 5)",
+                       "parallelism": f"tp{world} (N-sharded, output left vocab-parallel)",
+                       "l2": "inputs (1.9 GB/step) larger than L2"},
+            "gpu_launches": args.steps,
+            "roofline": {"bound": "tensor", "achieved": round(my_tflops, 2), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(my_tflops / peak, 4), "traffic": read_traffic("gemm_lmhead.txt"),
+                         "kernel": "hx_gemm_sm100_kernel", "peak_source": f"{peak_src} bf16_tflops"},
+            "clocks": clocks}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    """The reference's own CPU path on this box's host cores (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import cpu_reference as CR
+
+    n = cpu_threads()
+    torch.set_num_threads(n)
+    vals = CR.run_steps(args.workload, steps=args.steps, warmup=args.warmup, threads=n,
+                        budget_s=args.cpu_budget)
+    line = {"impl": "reference", "metric": vals["metric"], "value": vals["value"], "unit": vals["unit"],
+            "n_gpus": int(os.environ.get("WORLD_SIZE", args.gpus)), "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": vals["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": vals["dtype"], "data": "synthetic",
+            "config": vals["config"],
+            "cpu_baseline": {"value": vals["value"], "unit": vals["unit"], "cores": n, "kind": "port",
+                             "sample": vals["sample"]},
+            "e2e": {"value": vals["value"], "unit": vals["unit"], "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["hx", "reference"], default="hx")
+    ap.add_argument("--workload", choices=["gpt2", "qwen", "tinyllama", "lmhead"], default="gpt2")
+    ap.add_argument("--batch", type=int, default=1, help="decode batch M for --workload tinyllama")
+    ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU work for the CPU baseline")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_hx(args)
+
+
+if __name__ == "__main__":
+    main()

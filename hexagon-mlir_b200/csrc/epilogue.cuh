@@ -9,7 +9,7 @@
 //
 // Math follows the reference's golden (PyTorch): F.gelu(approximate="tanh")
 // (test/python/triton/test_gelu.py:72) and F.silu (test_silu.py:63), both
-// evaluated in fp32 with CUDA's expf/tanhf.
+// evaluated in fp32 (CUDA's __expf; GELU through an exact identity below).
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -30,6 +30,8 @@ struct EpiArgs {
   int32_t M, N;        // output extent (columns of C)
   int32_t c_vec_ok;    // C rows are 16-byte aligned: vector stores allowed
   int32_t r_vec_ok;    // residual rows are 16-byte aligned
+  int32_t b_vec_ok;    // bias is 16-byte aligned
+  int32_t s_vec_ok;    // scale is 16-byte aligned
 };
 
 __device__ __forceinline__ float ld_as_float(const void *p, int dtype, int64_t i) {
@@ -42,75 +44,87 @@ __device__ __forceinline__ float ld_as_float(const void *p, int dtype, int64_t i
   }
 }
 
+// GELU-tanh through the identity 0.5 * (1 + tanh(y)) = 1 / (1 + exp(-2y)):
+//   gelu_tanh(x) = x / (1 + exp(-2 * sqrt(2/pi) * (x + 0.044715 x^3)))
+// which needs one exponential (CUDA's __expf) and one fast division.
 __device__ __forceinline__ float gelu_tanh(float x) {
-  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
-  const float k0 = 0.7978845608028654f;
+  const float k0x2 = 1.5957691216057308f;  // 2 * sqrt(2/pi)
   const float k1 = 0.044715f;
-  return 0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x)));
+  const float y = k0x2 * fmaf(k1 * x, x * x, x);
+  return __fdividef(x, 1.f + __expf(-y));
 }
-__device__ __forceinline__ float silu(float x) { return x / (1.f + expf(-x)); }
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.f + __expf(-x)); }
+
+// Load 32 consecutive elements v[j] = p[n0 + j] as float, j < 32 (columns
+// >= N read as 0).  `vec_ok`: p is 16-byte aligned (n0 is a multiple of 32).
+__device__ __forceinline__ void load_row32(const void *p, int dtype, int64_t base, int n0, int N,
+                                           bool vec_ok, float (&v)[32]) {
+  if (vec_ok && n0 + 32 <= N && (dtype == HX_F16 || dtype == HX_BF16)) {
+    const uint4 *q = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(p) + base + n0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 w = __ldg(q + i);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        if (dtype == HX_F16) {
+          const __half2 t = *reinterpret_cast<const __half2 *>(&ws[h]);
+          v[i * 8 + 2 * h] = __low2float(t);
+          v[i * 8 + 2 * h + 1] = __high2float(t);
+        } else {
+          const __nv_bfloat162 t = *reinterpret_cast<const __nv_bfloat162 *>(&ws[h]);
+          v[i * 8 + 2 * h] = __low2float(t);
+          v[i * 8 + 2 * h + 1] = __high2float(t);
+        }
+      }
+    }
+    return;
+  }
+  if (vec_ok && n0 + 32 <= N && dtype == HX_F32) {
+    const float4 *q = reinterpret_cast<const float4 *>(static_cast<const float *>(p) + base + n0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 w = __ldg(q + i);
+      v[4 * i] = w.x;
+      v[4 * i + 1] = w.y;
+      v[4 * i + 2] = w.z;
+      v[4 * i + 3] = w.w;
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = (n0 + j < N) ? ld_as_float(p, dtype, base + n0 + j) : 0.f;
+}
 
 // Apply the epilogue to 32 consecutive output columns of one row.
 //   v[j]   : accumulator for column n0 + j (gate half for SWIGLU)
 //   up[j]  : "up" accumulator for SWIGLU (ignored otherwise)
+// Every switch below is on a value uniform across the CTA; the per-element
+// loops inside each case are straight-line code.
 __device__ __forceinline__ void epi_transform32(const EpiArgs &e, float (&v)[32],
                                                 const float (&up)[32], int m, int n0) {
-  const bool full = (n0 + 32 <= e.N);
   const int epi = e.epi;
+  if (epi == HX_EPI_NONE) return;
   if (epi == HX_EPI_SWIGLU) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = silu(v[j]) * up[j];
     return;
   }
+  float t[32];
   if (epi == HX_EPI_DEQUANT_SCALE) {
+    load_row32(e.scale, e.scale_dtype, 0, n0, e.N, e.s_vec_ok, t);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int n = (full || n0 + j < e.N) ? n0 + j : e.N - 1;
-      v[j] *= ld_as_float(e.scale, e.scale_dtype, n);
-    }
+    for (int j = 0; j < 32; ++j) v[j] *= t[j];
   }
-  const bool has_bias = e.bias != nullptr &&
-                        (epi == HX_EPI_BIAS || epi == HX_EPI_BIAS_GELU_TANH ||
-                         epi == HX_EPI_BIAS_RESIDUAL || epi == HX_EPI_DEQUANT_SCALE ||
-                         epi == HX_EPI_BIAS_SILU);
-  if (has_bias) {
+  if (e.bias != nullptr && epi != HX_EPI_RESIDUAL) {
+    load_row32(e.bias, e.bias_dtype, 0, n0, e.N, e.b_vec_ok, t);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int n = (full || n0 + j < e.N) ? n0 + j : e.N - 1;
-      v[j] += ld_as_float(e.bias, e.bias_dtype, n);
-    }
+    for (int j = 0; j < 32; ++j) v[j] += t[j];
   }
-  if ((epi == HX_EPI_BIAS_RESIDUAL || epi == HX_EPI_RESIDUAL) && e.residual != nullptr &&
-      m < e.M) {
-    const int64_t base = static_cast<int64_t>(m) * e.ldr + n0;
-    if (full && e.r_vec_ok && (e.c_dtype == HX_F16 || e.c_dtype == HX_BF16)) {
-      const uint4 *rp = reinterpret_cast<const uint4 *>(
-          static_cast<const uint16_t *>(e.residual) + base);
+  if ((epi == HX_EPI_BIAS_RESIDUAL || epi == HX_EPI_RESIDUAL) && m < e.M) {
+    load_row32(e.residual, e.c_dtype, static_cast<int64_t>(m) * e.ldr, n0, e.N, e.r_vec_ok, t);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint4 w = __ldg(rp + q);
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          float lo, hi;
-          if (e.c_dtype == HX_F16) {
-            const __half2 p = *reinterpret_cast<const __half2 *>(&ws[h]);
-            lo = __low2float(p);
-            hi = __high2float(p);
-          } else {
-            const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162 *>(&ws[h]);
-            lo = __low2float(p);
-            hi = __high2float(p);
-          }
-          v[q * 8 + h * 2] += lo;
-          v[q * 8 + h * 2 + 1] += hi;
-        }
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (n0 + j < e.N) v[j] += ld_as_float(e.residual, e.c_dtype, base + j);
-    }
+    for (int j = 0; j < 32; ++j) v[j] += t[j];
   }
   if (epi == HX_EPI_BIAS_GELU_TANH) {
 #pragma unroll

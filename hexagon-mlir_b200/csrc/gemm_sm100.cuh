@@ -14,12 +14,14 @@
 //   * the 4-thread scf.forall split (FormVirtualThreadsPass.cpp:51-202):
 //     a persistent grid of one CTA per SM walking a grouped tile order;
 //   * the unfused epilogue generic (FusionPass.cpp:163,176-179): applied to
-//     the accumulator in registers by four epilogue warps.
+//     the accumulator in registers by eight epilogue warps.
 //
-// Warp roles (192 threads):
+// Warp roles (320 threads):
 //   warp 0      TMA producer (lane 0 issues)
 //   warp 1      TMEM allocator + UMMA issuer (lane 0 issues)
-//   warps 2..5  epilogue: TMEM -> registers -> fused epilogue -> global
+//   warps 2..9  epilogue: TMEM -> registers -> fused epilogue -> global;
+//               warp w reads TMEM lane quarter w % 4 and every other
+//               32-column chunk ((w - 2) / 4 picks which)
 // TMEM holds two BN-column fp32/s32 accumulators so the epilogue of tile i
 // overlaps the mainloop of tile i+1.
 #pragma once
@@ -34,7 +36,8 @@ namespace hx {
 constexpr int kBM = 128;          // UMMA M (rows of A per tile)
 constexpr int kKBytes = 128;      // K bytes per stage (one 128B swizzle row)
 constexpr int kUmmaKBytes = 32;   // K bytes per UMMA instruction
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
 
 struct GemmParams {
   int32_t M, K;                   // rows of A/C, reduction length
@@ -112,7 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 4);
+      mbar_init(&tempty_bar[a], kEpiWarps);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -130,6 +133,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Prologue done: let the next kernel in the stream start its own, then
+  // wait for the previous one before reading or writing global memory.
+  grid_dep_launch_dependents();
+  grid_dep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -274,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = m_blk * kBM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 #pragma unroll 1
-      for (int c = 0; c < Cfg::kBNOut / 32; ++c) {
+      for (int c = (warp - 2) / 4; c < Cfg::kBNOut / 32; c += 2) {
         uint32_t r[32];
         uint32_t r2[32];
         tmem_ld_32x32b_x32(t_row + c * 32, r);

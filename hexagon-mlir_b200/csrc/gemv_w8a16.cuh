@@ -13,6 +13,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "ptx.cuh"
+
 namespace hx {
 
 struct GemvParams {
@@ -40,6 +42,8 @@ __device__ __forceinline__ void i8x4_to_f32(uint32_t w, float (&f)[4]) {
 template <int ROWS, int MC>
 __global__ void __launch_bounds__(128) hx_gemv_w8a16_kernel(const GemvParams p) {
   extern __shared__ __align__(16) __half xs[];  // [MC][K]
+  grid_dep_launch_dependents();
+  grid_dep_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = (blockIdx.x * 4 + warp) * ROWS;
   const int kvec = p.K / 16;

@@ -16,6 +16,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "gemm_simt.cuh"
 #include "gemm_sm100.cuh"
@@ -132,6 +133,25 @@ constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in limit per block on sm_100
 constexpr uint64_t kDefaultTimeout = 4000000000ull;  // ~2 s at 2 GHz
 
 // ------------------------------------------------------------ launch
+// Launch with programmatic stream serialization (PDL): the kernel may begin
+// while its predecessor finishes; it calls griddepcontrol.wait before its
+// first global-memory access, so ordering is unchanged.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 template <int BN, int KIND, bool BMN, bool SW>
 int launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p, int grid,
               cudaStream_t s) {
@@ -145,8 +165,8 @@ int launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     configured.store(kMaxDynSmem, std::memory_order_release);
   }
-  kern<<<grid, kThreads, smem, s>>>(ta, tb, p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, ta, tb, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "hx_gemm_sm100_kernel launch");
   return HX_OK;
 }
@@ -226,10 +246,11 @@ int validate(const hx_gemm_desc *d) {
   switch (d->epilogue) {
     case HX_EPI_NONE: break;
     case HX_EPI_BIAS:
-    case HX_EPI_BIAS_GELU_TANH:
-    case HX_EPI_BIAS_SILU:
       if (!d->bias) return arg_fail("epilogue needs bias");
       break;
+    case HX_EPI_BIAS_GELU_TANH:
+    case HX_EPI_BIAS_SILU:
+      break;  // bias optional (NULL = no bias)
     case HX_EPI_BIAS_RESIDUAL:
       if (!d->bias || !d->residual) return arg_fail("epilogue needs bias and residual");
       if (d->ldr < d->N) return arg_fail("ldr < N");
@@ -273,6 +294,8 @@ EpiArgs make_epi(const hx_gemm_desc *d) {
   const int cz = esize(d->c_dtype);
   e.c_vec_ok = aligned16(d->C) && ((d->ldc * cz) % 16 == 0);
   e.r_vec_ok = d->residual && aligned16(d->residual) && ((d->ldr * cz) % 16 == 0);
+  e.b_vec_ok = d->bias && aligned16(d->bias);
+  e.s_vec_ok = d->scale && aligned16(d->scale);
   return e;
 }
 
@@ -408,8 +431,8 @@ int gemv_impl(int64_t M, int64_t N, int64_t K, const void *x, int64_t ldx, const
         cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kMaxDynSmem);
         if (r != cudaSuccess) return r;
-        kern<<<static_cast<unsigned>(blocks), 128, static_cast<size_t>(smem), s>>>(p);
-        return cudaGetLastError();
+        r = launch_pdl(kern, dim3(static_cast<unsigned>(blocks)), dim3(128), static_cast<size_t>(smem), s, p);
+        return r == cudaSuccess ? cudaGetLastError() : r;
       };
       switch (mc) {
         case 1: e = launch(hx_gemv_w8a16_kernel<ROWS, 1>); break;

@@ -118,6 +118,18 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// ------------------------------------------------------- programmatic launch
+// With programmatic stream serialization the next kernel in the stream may
+// start while this one runs.  griddepcontrol.wait blocks until every
+// prerequisite grid has completed and its memory operations are visible;
+// launch_dependents lets the dependent grid start being scheduled.
+__device__ __forceinline__ void grid_dep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 // TMEM allocation is warp-wide (.sync.aligned): call from all 32 lanes.
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {

@@ -186,12 +186,12 @@ def linear(
         else:
             epi = "none"
     elif activation == "gelu_tanh":
-        if residual is not None or bias is None:
-            raise ValueError("gelu_tanh epilogue takes a bias and no residual")
+        if residual is not None:
+            raise ValueError("gelu_tanh epilogue takes no residual")
         epi = "bias_gelu_tanh"
     elif activation == "silu":
-        if residual is not None or bias is None:
-            raise ValueError("silu epilogue takes a bias and no residual")
+        if residual is not None:
+            raise ValueError("silu epilogue takes no residual")
         epi = "bias_silu"
     elif activation == "swiglu":
         if residual is not None or bias is not None:

@@ -65,13 +65,13 @@ extern "C" {
 /* ---- fused epilogues (the linalg.generic ops that follow the matmul) ---- */
 #define HX_EPI_NONE 0           /* C = acc                                     */
 #define HX_EPI_BIAS 1           /* C = acc + bias[n]                           */
-#define HX_EPI_BIAS_GELU_TANH 2 /* C = gelu_tanh(acc + bias[n])                */
+#define HX_EPI_BIAS_GELU_TANH 2 /* C = gelu_tanh(acc + bias[n]); bias optional */
 #define HX_EPI_BIAS_RESIDUAL 3  /* C = acc + bias[n] + R[m,n]                  */
 #define HX_EPI_RESIDUAL 4       /* C = acc + R[m,n]                            */
 #define HX_EPI_SWIGLU 5         /* C = silu(acc_gate) * acc_up; B holds 2N rows:
                                    rows [0,N) gate, rows [N,2N) up (HX_B_NK)   */
 #define HX_EPI_DEQUANT_SCALE 6  /* C = acc * scale[n] (+ bias[n] if given)     */
-#define HX_EPI_BIAS_SILU 7      /* C = silu(acc + bias[n])                     */
+#define HX_EPI_BIAS_SILU 7      /* C = silu(acc + bias[n]); bias optional      */
 
 /* Problem descriptor for hx_gemm().  Zero-initialise and fill what applies. */
 typedef struct hx_gemm_desc {

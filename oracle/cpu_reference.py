@@ -1,0 +1,127 @@
+"""The reference's CPU path for each benchmark workload, timed on the host
+cores — TEST / BENCHMARK INFRASTRUCTURE ONLY (bench.py's CPU-baseline and
+`--impl reference` legs).
+
+The reference checks every matmul against PyTorch on the host CPU
+(test/python/triton/test_matmul.py:90 `torch.matmul`,
+test/python/torch-mlir/utils.py:54 the model's PyTorch forward,
+benchmark_models/run_gpt2lmheadmodel.py:17-19 x86 logits).  With no
+Hexagon SDK/simulator available offline, that CPU golden is the reference's
+only runnable implementation of this path, so it is what the CPU legs time:
+PyTorch-CPU F.linear + epilogue in the workload's dtype (the same nn.Module
+the GPU path compiles), dequantise + fp32 F.linear for W8A16.
+
+Each measurement is a bounded sample (whole layers, or a block of LM-head
+rows) scaled to the workload's metric; the sample is described in the
+result.
+"""
+
+from __future__ import annotations
+
+import time
+
+import torch
+import torch.nn.functional as F
+
+from qcom_hexagon_backend import workloads as WL  # plain nn.Module definitions only
+
+
+def _timeit(fn, reps):
+    fn()  # warm-up
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        fn()
+        ts.append(time.perf_counter() - t0)
+    ts.sort()
+    return ts[len(ts) // 2]
+
+
+def _gpt2(budget_s):
+    model = WL.GPT2LinearStack().half()
+    g = torch.Generator().manual_seed(1234)
+    x = torch.randn(1024, 768, generator=g).half()
+    blk = model.blocks[0]
+    with torch.no_grad():
+        t1 = _timeit(lambda: blk(x), 2)
+        layers = max(1, min(12, int(budget_s / 6 / max(t1, 1e-6))))
+        sub = torch.nn.Sequential(*model.blocks[:layers])
+        t = _timeit(lambda: sub(x), 5)
+    flops = WL.gpt2_stack_flops(layers=layers)
+    return dict(metric="GEMM+epilogue TFLOP/s", unit="TFLOP/s", dtype="fp16",
+                value=round(flops / t / 1e12, 4), ms_per_step=round(t * 1e3 * 12 / layers, 3),
+                sample=f"PyTorch-CPU fp16 forward of {layers} of 12 GPT-2 linear layers "
+                       f"(M=1024), median of 5, scaled per layer",
+                config={"workload": "gpt2-small linear stack (BASELINE config 2)", "layers_timed": layers})
+
+
+def _qwen(budget_s):
+    model = WL.QwenLinearStack().to(torch.bfloat16)
+    g = torch.Generator().manual_seed(1235)
+    x = torch.randn(2048, 896, generator=g).to(torch.bfloat16)
+    blk = model.blocks[0]
+    acc = x.new_zeros(2048, blk.qkv.out_features)
+    with torch.no_grad():
+        t = _timeit(lambda: blk(x, acc), 5)
+    flops = WL.qwen_stack_flops(layers=1)
+    return dict(metric="GEMM+epilogue TFLOP/s", unit="TFLOP/s", dtype="bf16",
+                value=round(flops / t / 1e12, 4), ms_per_step=round(t * 1e3 * 24, 3),
+                sample="PyTorch-CPU bf16 forward of 1 of 24 Qwen2.5-0.5B linear layers (M=2048), median of 5",
+                config={"workload": "qwen2.5-0.5b prefill linear stack (BASELINE config 3)", "layers_timed": 1})
+
+
+def _tinyllama(budget_s, M=1):
+    layers = WL.make_tinyllama_w8a16(layers=1)
+    g = torch.Generator().manual_seed(1237)
+    x = torch.randn(M, 2048, generator=g).half()
+    xi = torch.randn(M, 5632, generator=g).half()
+
+    def step():
+        for p in WL.TINYLLAMA_PROJ:
+            l = layers[0][p]
+            wd = l.weight.float() * l.scale.float()[:, None]
+            F.linear((xi if p == "down" else x).float(), wd).half()
+
+    t = _timeit(step, 5)
+    nbytes = WL.tinyllama_decode_bytes(M, layers=1)
+    return dict(metric="W8A16 decode HBM GB/s", unit="GB/s", dtype="int8 x f16 (f32 acc)",
+                value=round(nbytes / t / 1e9, 3), ms_per_step=round(t * 1e3 * 22, 3),
+                sample=f"PyTorch-CPU dequantise + fp32 F.linear, 1 of 22 TinyLlama layers, M={M}, median of 5",
+                config={"workload": f"tinyllama-1.1b decode linears W8A16 M={M} (BASELINE config 4)"})
+
+
+def _lmhead(budget_s):
+    rows = 256
+    g = torch.Generator().manual_seed(1238)
+    a = torch.randn(rows, WL.LMHEAD_K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(WL.LMHEAD_N, WL.LMHEAD_K, generator=g) * 0.02).to(torch.bfloat16)
+    with torch.no_grad():
+        t = _timeit(lambda: F.linear(a, w), 3)
+    flops = 2.0 * rows * WL.LMHEAD_K * WL.LMHEAD_N
+    full = t * WL.LMHEAD_M / rows
+    return dict(metric="GEMM+epilogue TFLOP/s", unit="TFLOP/s", dtype="bf16",
+                value=round(flops / t / 1e12, 4), ms_per_step=round(full * 1e3, 3),
+                sample=f"PyTorch-CPU bf16 F.linear on {rows} of 16384 LM-head rows, median of 3, scaled",
+                config={"workload": "LM head 16384x2048x50304 bf16 (BASELINE config 5)"})
+
+
+_TABLE = {"gpt2": _gpt2, "qwen": _qwen, "tinyllama": _tinyllama, "lmhead": _lmhead}
+
+
+def time_workload(workload, budget_s=15.0, threads=1):
+    r = _TABLE[workload](budget_s)
+    return r["value"], r["unit"], r["sample"], threads
+
+
+def run_steps(workload, steps, warmup, threads, budget_s=15.0):
+    """`--impl reference`: the bounded CPU sample, measured once per step."""
+    vals = []
+    last = None
+    per = max(2.0, budget_s / max(1, steps + warmup))
+    for i in range(steps + warmup):
+        last = _TABLE[workload](per)
+        if i >= warmup:
+            vals.append(last["value"])
+    last["value"] = round(sorted(vals)[len(vals) // 2], 4)
+    last["sample"] += f"; {steps} steps after {warmup} warm-up, median"
+    return last
