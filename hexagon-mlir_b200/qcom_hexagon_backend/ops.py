@@ -84,6 +84,22 @@ def gemm(
     For epilogue "swiglu", b is the fused [gate; up] weight of 2N rows and
     out = silu(a @ gate.T) * (a @ up.T) has N columns.
     """
+    d, out, dev = make_desc(a, b, b_layout=b_layout, out=out, out_dtype=out_dtype, epilogue=epilogue,
+                            bias=bias, residual=residual, scale=scale, tile_n=tile_n, stages=stages,
+                            max_ctas=max_ctas, force_simt=force_simt, error_flag=error_flag,
+                            timeout_cycles=timeout_cycles)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.hx_gemm(ctypes.byref(d), ctypes.c_void_p(_stream_ptr(dev)))
+    _lib.check(rc, "hx_gemm")
+    return out
+
+
+def make_desc(a, b, *, b_layout="nk", out=None, out_dtype=None, epilogue="none", bias=None,
+              residual=None, scale=None, tile_n=0, stages=0, max_ctas=0, force_simt=False,
+              error_flag=None, timeout_cycles=0):
+    """Validate the tensors and fill an hx_gemm_desc; returns (desc, out, device).
+    The tensors must stay alive while the descriptor is in use."""
     _check_cuda(a, "a")
     dev = a.device
     _check_cuda(b, "b", dev)
@@ -151,11 +167,7 @@ def gemm(
             raise ValueError("error_flag must be an int32 CUDA tensor")
         d.error_flag = error_flag.data_ptr()
     d.timeout_cycles = timeout_cycles
-    lib = _lib.load()
-    with torch.cuda.device(dev):
-        rc = lib.hx_gemm(ctypes.byref(d), ctypes.c_void_p(_stream_ptr(dev)))
-    _lib.check(rc, "hx_gemm")
-    return out
+    return d, out, dev
 
 
 def linear(
