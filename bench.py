@@ -337,7 +337,7 @@ def run_tinyllama(args, world, rank, dev, peaks, peak_src):
     """Config 4: W8A16 decode linears, 22 layers x 7 projections, M in {1,8,32,64}."""
     from qcom_hexagon_backend import ops
 
-    layers = WL.make_tinyllama_w8a16()
+    layers = WL.make_tinyllama_w8a16(layers=args.layers)
     dl = [{p: (l[p].weight.to(dev), l[p].scale.to(dev)) for p in l} for l in layers]
     M = args.batch
     g = torch.Generator().manual_seed(1237)
@@ -346,11 +346,19 @@ def run_tinyllama(args, world, rank, dev, peaks, peak_src):
     outs = {p: torch.empty(M, WL.tinyllama_shapes()[p][0], dtype=torch.float16, device=dev)
             for p in WL.TINYLLAMA_PROJ}
 
+    # One persistent grouped launch per decode step (154 projections); each
+    # projection writes its own output buffer.
+    grp = ops.W8A16Group(M, dev)
+    ys = []
+    for l in dl:
+        for p in WL.TINYLLAMA_PROJ:
+            w, s = l[p]
+            y = torch.empty(M, w.shape[0], dtype=torch.float16, device=dev)
+            ys.append(y)
+            grp.add(xi if p == "down" else x, w, s, y)
+
     def step():
-        for l in dl:
-            for p in WL.TINYLLAMA_PROJ:
-                w, s = l[p]
-                ops.gemv_w8a16(xi if p == "down" else x, w, s, out=outs[p])
+        grp.run()
 
     step()
     torch.cuda.synchronize(dev)
@@ -376,18 +384,18 @@ def run_tinyllama(args, world, rank, dev, peaks, peak_src):
     clocks = clk.stop()
     total = max_over_ranks(sum(s.elapsed_time(e) for s, e in evs), world, dev)
     ms = total / args.steps
-    nbytes = WL.tinyllama_decode_bytes(M)
+    nbytes = WL.tinyllama_decode_bytes(M, layers=args.layers)
     gbs = nbytes / (ms / 1e3) / 1e9
     peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
     line = {"metric": "W8A16 decode HBM GB/s", "value": round(gbs * world, 1), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8 x f16 (f32 acc)", "data": "synthetic",
             "config": {"workload": f"tinyllama-1.1b decode linears W8A16 M={M} (BASELINE config 4)",
-                       "layers": 22, "M": M, "bytes_per_step": nbytes, "l2": "flushed before every step",
+                       "layers": args.layers, "M": M, "bytes_per_step": nbytes, "l2": "flushed before every step",
                        "parallelism": f"replicas{world}"},
-            "gpu_launches": 22 * 7 * args.steps,
+            "gpu_launches": args.steps,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(gbs / peak, 4), "traffic": None, "kernel": "hx_gemv_w8a16_kernel",
+                         "frac": round(gbs / peak, 4), "traffic": None, "kernel": "hx_gemv_w8a16_grouped_kernel",
                          "peak_source": f"{peak_src} hbm_gbs"},
             "clocks": clocks}
     if rank == 0:
@@ -479,6 +487,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["hx", "reference"], default="hx")
     ap.add_argument("--workload", choices=["gpt2", "qwen", "tinyllama", "lmhead"], default="gpt2")
     ap.add_argument("--batch", type=int, default=1, help="decode batch M for --workload tinyllama")
+    ap.add_argument("--layers", type=int, default=22, help="decoder layers for --workload tinyllama")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU work for the CPU baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)

@@ -13,6 +13,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -20,7 +21,9 @@
 
 #include "gemm_simt.cuh"
 #include "gemm_sm100.cuh"
+#include "gemv_grouped.cuh"
 #include "gemv_w8a16.cuh"
+#include "w8a16_sm100.cuh"
 #include "hx_gemm.h"
 
 #define HX_VERSION 1
@@ -397,8 +400,96 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------ W8A16
+// Tensor-core W8A16 (swap-AB, cluster split-K).  Returns HX_E_UNSUPPORTED
+// when the shape is outside what the kernel takes, so the caller can use
+// the CUDA-core kernels instead.
+template <int MPAD>
+int launch_w8a16_tc(const CUtensorMap &tw, const CUtensorMap &tx, const W8A16Params &p, int grid,
+                    cudaStream_t s) {
+  auto kern = hx_w8a16_tc_kernel<MPAD>;
+  const int smem = W8Cfg<MPAD>::smem_bytes(p.stages);
+  static std::atomic<int> configured{0};
+  if (!configured.load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w8a16)");
+    configured.store(1, std::memory_order_release);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kW8Threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tx, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "hx_w8a16_tc_kernel launch");
+  return HX_OK;
+}
+
+int w8a16_tc(int64_t M, int64_t N, int64_t K, const void *x, int64_t ldx, const int8_t *W,
+             int64_t ldw, const void *scale, const void *bias, void *y, int64_t ldy, int flags,
+             cudaStream_t s) {
+  if (M > 256 || K == 0 || ldw % 16 != 0 || ldx % 8 != 0 || !aligned16(x) || !aligned16(W))
+    return HX_E_UNSUPPORTED;
+  int sms = 0, major = 0;
+  int rc = current_device_info(&sms, &major);
+  if (rc != HX_OK) return rc;
+  if (major != 10) {
+    g_last_error = "current device is not sm_100";
+    return HX_E_NO_DEVICE;
+  }
+  const int mpad = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256)));
+  CUtensorMap tw, tx;
+  rc = make_tmap(&tw, W, HX_S8, K, N, ldw, kW8KBlock, 128);
+  if (rc != HX_OK) return rc;
+  rc = make_tmap(&tx, x, HX_F16, K, M, ldx, 64, mpad);
+  if (rc != HX_OK) return rc;
+  W8A16Params p;
+  p.M = static_cast<int32_t>(M);
+  p.N = static_cast<int32_t>(N);
+  p.K = static_cast<int32_t>(K);
+  p.k_blocks = static_cast<int32_t>((K + kW8KBlock - 1) / kW8KBlock);
+  const int64_t n_tiles = (N + 127) / 128;
+  // Cluster size: enough CTAs to cover the SMs in one wave, at most 4 (so
+  // clusters place easily next to a previous kernel's CTAs).
+  int splits = static_cast<int>(std::min<int64_t>(4, std::max<int64_t>(1, sms / n_tiles)));
+  if (const char *env = std::getenv("HX_W8A16_SPLITS")) splits = std::atoi(env);  // tuning override
+  splits = std::max(1, std::min(std::min(splits, 8), p.k_blocks));
+  if (n_tiles * splits > INT32_MAX) return unsupported("size");
+  p.splits = splits;
+  const int stage_bytes = 128 * 128 * 3 + 2 * mpad * 128;
+  // Two stages keep a CTA near 100 KB so two fit on an SM (a decode GEMM and
+  // the next one, launched early, side by side).
+  p.stages = 2;
+  if (const char *env = std::getenv("HX_W8A16_STAGES")) p.stages = std::atoi(env);  // tuning override
+  p.stages = std::max(2, std::min(p.stages, (kMaxDynSmem - 1280) / stage_bytes));
+  p.weights_const = (flags & HX_GEMV_WEIGHTS_CONST) ? 1 : 0;
+  p.scale = static_cast<const __half *>(scale);
+  p.bias = static_cast<const __half *>(bias);
+  p.y = static_cast<__half *>(y);
+  p.ldy = ldy;
+  p.timeout = kDefaultTimeout;
+  p.err_flag = nullptr;
+  const int grid = static_cast<int>(n_tiles * splits);
+  switch (mpad) {
+    case 16: return launch_w8a16_tc<16>(tw, tx, p, grid, s);
+    case 32: return launch_w8a16_tc<32>(tw, tx, p, grid, s);
+    case 64: return launch_w8a16_tc<64>(tw, tx, p, grid, s);
+    case 128: return launch_w8a16_tc<128>(tw, tx, p, grid, s);
+    default: return launch_w8a16_tc<256>(tw, tx, p, grid, s);
+  }
+}
+
 int gemv_impl(int64_t M, int64_t N, int64_t K, const void *x, int64_t ldx, const int8_t *W,
-              int64_t ldw, const void *scale, const void *bias, void *y, int64_t ldy,
+              int64_t ldw, const void *scale, const void *bias, void *y, int64_t ldy, int flags,
               cudaStream_t s) {
   if (M < 0 || N < 0 || K < 0) return arg_fail("negative size");
   if (M == 0 || N == 0) return HX_OK;
@@ -417,6 +508,40 @@ int gemv_impl(int64_t M, int64_t N, int64_t K, const void *x, int64_t ldx, const
   p.bias = static_cast<const __half *>(bias);
   p.y = static_cast<__half *>(y);
   p.ldy = ldy;
+  const bool vec_ok = K > 0 && K % 16 == 0 && ldw % 16 == 0 && ldx % 8 == 0 && aligned16(x) &&
+                      aligned16(W);
+  if (vec_ok && M <= 8 && !(flags & HX_GEMV_FORCE_CUDA_CORE)) {
+    // Streaming CUDA-core kernel: R rows x K int8 per CTA, up to 48 KB.
+    int R = K <= 1536 ? 32 : (K <= 3072 ? 16 : 8);
+    if (static_cast<int64_t>(R) * K <= 48 * 1024) {
+      GemvStreamParams sp;
+      sp.g = p;
+      sp.rows_per_cta = R;
+      sp.weights_const = (flags & HX_GEMV_WEIGHTS_CONST) ? 1 : 0;
+      sp.timeout = kDefaultTimeout;
+      const size_t smem = static_cast<size_t>(R) * K + 16;
+      const int64_t blocks = (N + R - 1) / R;
+      auto launch = [&](auto kern) -> cudaError_t {
+        cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kMaxDynSmem);
+        if (r != cudaSuccess) return r;
+        r = launch_pdl(kern, dim3(static_cast<unsigned>(blocks)), dim3(256), smem, s, sp);
+        return r == cudaSuccess ? cudaGetLastError() : r;
+      };
+      cudaError_t e;
+      if (M <= 1) e = launch(hx_gemv_w8a16_stream_kernel<1>);
+      else if (M <= 2) e = launch(hx_gemv_w8a16_stream_kernel<2>);
+      else if (M <= 4) e = launch(hx_gemv_w8a16_stream_kernel<4>);
+      else e = launch(hx_gemv_w8a16_stream_kernel<8>);
+      if (e != cudaSuccess) return cuda_fail(e, "hx_gemv_w8a16_stream_kernel");
+      return HX_OK;
+    }
+  }
+  if (!(flags & HX_GEMV_FORCE_CUDA_CORE)) {
+    const int rc = w8a16_tc(M, N, K, x, ldx, W, ldw, scale, bias, y, ldy, flags, s);
+    if (rc != HX_E_UNSUPPORTED) return rc;
+    g_last_error.clear();
+  }
   const bool vec = K > 0 && K % 16 == 0 && ldw % 16 == 0 && ldx % 8 == 0 && aligned16(x) &&
                    aligned16(W);
   cudaError_t e;
@@ -450,6 +575,86 @@ int gemv_impl(int64_t M, int64_t N, int64_t K, const void *x, int64_t ldx, const
   hx_gemv_w8a16_scalar_kernel<<<static_cast<unsigned>(blocks), 128, 0, s>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "hx_gemv_w8a16_scalar_kernel");
+  return HX_OK;
+}
+
+// ------------------------------------------------------------ grouped W8A16
+int gemv_grouped_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32_t *counters,
+                      int32_t *error_flag, cudaStream_t s) {
+  if (M < 0 || count < 0) return arg_fail("negative size");
+  if (count == 0 || M == 0) return HX_OK;
+  if (count > kGroupMax) return unsupported("more projections than one grouped launch takes (256)");
+  if (M > 8) return unsupported("grouped W8A16 takes M <= 8");
+  if (!projs || !counters) return arg_fail("null projections or counters");
+  int sms = 0, major = 0;
+  int rc = current_device_info(&sms, &major);
+  if (rc != HX_OK) return rc;
+  if (major != 10) {
+    g_last_error = "current device is not sm_100";
+    return HX_E_NO_DEVICE;
+  }
+  static GroupParams p;  // 18 KB: built on the host, passed by value at launch
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  p.G = count;
+  p.M = static_cast<int32_t>(M);
+  p.counters = counters;
+  p.err_flag = error_flag;
+  p.timeout = kDefaultTimeout;
+  int64_t items = 0;
+  for (int g = 0; g < count; ++g) {
+    const hx_w8a16_proj &q = projs[g];
+    if (q.N <= 0 || q.K <= 0 || !q.x || !q.W || !q.scale || !q.y) return arg_fail("bad projection");
+    if (q.ldx < q.K || q.ldw < q.K || q.ldy < q.N) return arg_fail("leading dimension too small");
+    if (q.N > INT32_MAX || q.K > INT32_MAX || q.ldx > INT32_MAX || q.ldw > INT32_MAX || q.ldy > INT32_MAX)
+      return unsupported("size");
+    if (q.dep >= g || q.dep < -1) return arg_fail("dep must name an earlier projection or be -1");
+    if (q.K % 16 || q.ldw % 16 || q.ldx % 8 || !aligned16(q.x) || !aligned16(q.W))
+      return unsupported("grouped W8A16 needs K % 16 == 0 and 16-byte aligned rows");
+    int R = M <= 2 ? 16 : 8;  // rows per item; 8 compute warps take R / 8 each
+    while (R > 8 && static_cast<int64_t>(R) * q.K > kGroupSlotBytes) R >>= 1;
+    if (static_cast<int64_t>(R) * q.K > kGroupSlotBytes) return unsupported("K too large for a slot");
+    GroupDesc &d = p.d[g];
+    d.W = q.W;
+    d.scale = static_cast<const __half *>(q.scale);
+    d.bias = static_cast<const __half *>(q.bias);
+    d.x = static_cast<const __half *>(q.x);
+    d.y = static_cast<__half *>(q.y);
+    d.N = static_cast<int32_t>(q.N);
+    d.K = static_cast<int32_t>(q.K);
+    d.ldw = static_cast<int32_t>(q.ldw);
+    d.ldx = static_cast<int32_t>(q.ldx);
+    d.ldy = static_cast<int32_t>(q.ldy);
+    d.dep = q.dep;
+    d.item_begin = static_cast<int32_t>(items);
+    d.rows = R;
+    d.signal = 0;
+    d.x_in_slot = ((static_cast<int64_t>(R) * q.K + 15) / 16) * 16 + M * q.K * 2 <= kGroupSlotBytes &&
+                  (q.ldx * 2) % 16 == 0;
+    if (q.dep >= 0) p.d[q.dep].signal = 1;
+    items += (q.N + R - 1) / R;
+    if (items > INT32_MAX) return unsupported("too many items");
+  }
+  p.total_items = static_cast<int32_t>(items);
+  cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int32_t) * count, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(counters)");
+  const int grid = static_cast<int>(std::min<int64_t>(items, 2 * sms));  // two CTAs per SM
+  const int mc = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
+  const size_t smem =
+      kGroupSlots * kGroupSlotBytes + 16 * kGroupSlots + 64;
+  auto launch = [&](auto kern) -> cudaError_t {
+    // dynamic + static shared memory must stay within the 227 KB per block
+    cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (r != cudaSuccess) return r;
+    r = launch_pdl(kern, dim3(grid), dim3(kGroupThreads + 32), smem, s, p);
+    return r == cudaSuccess ? cudaGetLastError() : r;
+  };
+  if (M <= 1) e = launch(hx_gemv_w8a16_grouped_kernel<1, 2>);
+  else if (M <= 2) e = launch(hx_gemv_w8a16_grouped_kernel<2, 2>);
+  else if (M <= 4) e = launch(hx_gemv_w8a16_grouped_kernel<4, 1>);
+  else e = launch(hx_gemv_w8a16_grouped_kernel<8, 1>);
+  if (e != cudaSuccess) return cuda_fail(e, "hx_gemv_w8a16_grouped_kernel");
   return HX_OK;
 }
 
@@ -576,8 +781,24 @@ int hx_gemv_w8a16(int64_t M, int64_t N, int64_t K, const void *x, int64_t ldx, c
                   int64_t ldw, const void *scale, const void *bias, void *y, int64_t ldy,
                   void *stream) {
   hx::g_last_error.clear();
-  return hx::gemv_impl(M, N, K, x, ldx, W, ldw, scale, bias, y, ldy,
+  return hx::gemv_impl(M, N, K, x, ldx, W, ldw, scale, bias, y, ldy, 0,
                        static_cast<cudaStream_t>(stream));
+}
+
+int hx_gemv_w8a16_ex(int64_t M, int64_t N, int64_t K, const void *x, int64_t ldx,
+                     const int8_t *W, int64_t ldw, const void *scale, const void *bias, void *y,
+                     int64_t ldy, int flags, void *stream) {
+  hx::g_last_error.clear();
+  if (flags & ~(HX_GEMV_WEIGHTS_CONST | HX_GEMV_FORCE_CUDA_CORE)) return HX_E_INVALID_ARG;
+  return hx::gemv_impl(M, N, K, x, ldx, W, ldw, scale, bias, y, ldy, flags,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int hx_gemv_w8a16_grouped(int64_t M, int count, const hx_w8a16_proj *projs, int32_t *counters,
+                          int32_t *error_flag, void *stream) {
+  hx::g_last_error.clear();
+  return hx::gemv_grouped_impl(M, count, projs, counters, error_flag,
+                               static_cast<cudaStream_t>(stream));
 }
 
 int hx_query_workspace(const hx_gemm_desc *d, int64_t *bytes) {

@@ -8,6 +8,7 @@ lib/libhx_gemm.so instead of the MLIR -> Hexagon LLVM -> DSP pipeline.
 """
 
 from . import _lib
-from .ops import gemm, gemv_w8a16, linear, matmul, matmul_f16f16_f32, shards_to_rows
+from . import ops
+from .ops import W8A16Group, gemm, gemv_w8a16, linear, matmul, matmul_f16f16_f32, shards_to_rows
 
 __all__ = ["gemm", "gemv_w8a16", "linear", "matmul", "matmul_f16f16_f32", "shards_to_rows", "_lib"]

@@ -32,6 +32,9 @@ HX_E_TOO_LARGE = -7
 HX_F16, HX_BF16, HX_S8, HX_S32, HX_F32 = 0, 1, 2, 3, 4
 # B layouts
 HX_B_NK, HX_B_KN = 0, 1
+# hx_gemv_w8a16_ex flags
+HX_GEMV_WEIGHTS_CONST = 1
+HX_GEMV_FORCE_CUDA_CORE = 2
 # epilogues
 HX_EPI_NONE = 0
 HX_EPI_BIAS = 1
@@ -87,12 +90,27 @@ class HxGemmDesc(ctypes.Structure):
     ]
 
 
+class HxW8A16Proj(ctypes.Structure):
+    """Mirror of `hx_w8a16_proj`."""
+
+    _fields_ = [
+        ("N", ctypes.c_int64), ("K", ctypes.c_int64),
+        ("x", ctypes.c_void_p), ("ldx", ctypes.c_int64),
+        ("W", ctypes.c_void_p), ("ldw", ctypes.c_int64),
+        ("scale", ctypes.c_void_p), ("bias", ctypes.c_void_p),
+        ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64),
+        ("dep", ctypes.c_int32), ("reserved", ctypes.c_int32),
+    ]
+
+
 # Every function the header declares, with its ctypes signature.
 _I64, _I32, _VP = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
 SIGNATURES = {
     "hx_gemm": (_I32, [ctypes.POINTER(HxGemmDesc), _VP]),
     "hx_matmul_f16f16_f32": (_I32, [_I64, _I64, _I64, _VP, _VP, _VP, _VP]),
     "hx_gemv_w8a16": (_I32, [_I64, _I64, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _VP, _I64, _VP]),
+    "hx_gemv_w8a16_ex": (_I32, [_I64, _I64, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _VP, _I64, _I32, _VP]),
+    "hx_gemv_w8a16_grouped": (_I32, [_I64, _I32, ctypes.POINTER(HxW8A16Proj), _VP, _VP, _VP]),
     "hx_sharded_gemm_allgather": (_I32, [ctypes.POINTER(HxGemmDesc), _I32, _I32, _VP, _VP, _VP]),
     "hx_shards_to_rows": (_I32, [_VP, _VP, _I32, _I64, _I64, _I32, _VP]),
     "hx_nccl_unique_id_size": (_I32, []),

@@ -246,8 +246,12 @@ def matmul_f16f16_f32(act: torch.Tensor, w: torch.Tensor, out: Optional[torch.Te
 
 
 def gemv_w8a16(x: torch.Tensor, w_int8: torch.Tensor, scale: torch.Tensor,
-               bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """y[M,N] = x[M,K] @ (w_int8[N,K] * scale[N,None]).T (+ bias), f16 in/out."""
+               bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None, *,
+               weights_const: bool = False, force_cuda_core: bool = False) -> torch.Tensor:
+    """y[M,N] = x[M,K] @ (w_int8[N,K] * scale[N,None]).T (+ bias), f16 in/out.
+
+    weights_const: the weight/scale are model constants that no kernel still
+    running before this call writes; their loads then overlap that kernel."""
     _check_cuda(x, "x")
     dev = x.device
     _check_cuda(w_int8, "w_int8", dev)
@@ -271,13 +275,69 @@ def gemv_w8a16(x: torch.Tensor, w_int8: torch.Tensor, scale: torch.Tensor,
     o2 = out.reshape(-1, N)
     lib = _lib.load()
     with torch.cuda.device(dev):
-        rc = lib.hx_gemv_w8a16(
+        flags = (_lib.HX_GEMV_WEIGHTS_CONST if weights_const else 0) | (
+            _lib.HX_GEMV_FORCE_CUDA_CORE if force_cuda_core else 0)
+        rc = lib.hx_gemv_w8a16_ex(
             M, N, K, x2.data_ptr(), _row_major_2d(x2, "x"), w_int8.data_ptr(),
             _row_major_2d(w_int8, "w_int8"), scale.data_ptr(),
             bias.data_ptr() if bias is not None else None, o2.data_ptr(),
-            _row_major_2d(o2, "out"), ctypes.c_void_p(_stream_ptr(dev)))
+            _row_major_2d(o2, "out"), flags, ctypes.c_void_p(_stream_ptr(dev)))
     _lib.check(rc, "hx_gemv_w8a16")
     return out.reshape(*lead, N)
+
+
+class W8A16Group:
+    """A list of W8A16 projections run as one persistent launch
+    (hx_gemv_w8a16_grouped): the linears of a decode step.
+
+    add() returns the projection's index; pass it as `dep` of a later
+    projection whose x is that projection's y.  run() launches the group on
+    the current stream.  All tensors must stay alive while the group is used.
+    """
+
+    def __init__(self, M: int, device):
+        self.M = M
+        self.device = torch.device(device)
+        self._items = []
+        self._keep = []
+        self._arr = None
+        self.counters = None
+        self.error_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def add(self, x, w_int8, scale, y, bias=None, dep: int = -1) -> int:
+        for t, nm in ((x, "x"), (w_int8, "w_int8"), (scale, "scale"), (y, "y")):
+            _check_cuda(t, nm, self.device)
+        if x.dtype != torch.float16 or y.dtype != torch.float16 or w_int8.dtype != torch.int8:
+            raise TypeError("W8A16 projection takes f16 x/y and an int8 weight")
+        N, K = w_int8.shape
+        if tuple(x.shape) != (self.M, K) or tuple(y.shape) != (self.M, N) or scale.numel() != N:
+            raise ValueError("projection shapes do not match M, N, K")
+        if not (-1 <= dep < len(self._items)):
+            raise ValueError("dep must be -1 or the index of an earlier projection")
+        it = _lib.HxW8A16Proj()
+        it.N, it.K = N, K
+        it.x, it.ldx = x.data_ptr(), _row_major_2d(x, "x")
+        it.W, it.ldw = w_int8.data_ptr(), _row_major_2d(w_int8, "w_int8")
+        it.scale = scale.data_ptr()
+        it.bias = bias.data_ptr() if bias is not None else None
+        it.y, it.ldy = y.data_ptr(), _row_major_2d(y, "y")
+        it.dep = dep
+        self._items.append(it)
+        self._keep += [x, w_int8, scale, y, bias]
+        self._arr = None
+        return len(self._items) - 1
+
+    def run(self):
+        n = len(self._items)
+        if self._arr is None:
+            self._arr = (_lib.HxW8A16Proj * n)(*self._items)
+            self.counters = torch.zeros(max(n, 1), dtype=torch.int32, device=self.device)
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            rc = lib.hx_gemv_w8a16_grouped(self.M, n, self._arr, ctypes.c_void_p(self.counters.data_ptr()),
+                                           ctypes.c_void_p(self.error_flag.data_ptr()),
+                                           ctypes.c_void_p(_stream_ptr(self.device)))
+        _lib.check(rc, "hx_gemv_w8a16_grouped")
 
 
 def shards_to_rows(gathered: torch.Tensor, world: int) -> torch.Tensor:

@@ -130,6 +130,51 @@ int hx_gemv_w8a16(int64_t M, int64_t N, int64_t K, const void *x, int64_t ldx,
                   const int8_t *W, int64_t ldw, const void *scale,
                   const void *bias, void *y, int64_t ldy, void *stream);
 
+/* Flags for hx_gemv_w8a16_ex. */
+#define HX_GEMV_WEIGHTS_CONST 1   /* W and scale are constant: nothing still
+                                     running before this call in the stream
+                                     writes them, so their loads may start
+                                     before the previous kernel finishes */
+#define HX_GEMV_FORCE_CUDA_CORE 2 /* use the CUDA-core kernel (validation) */
+
+/* hx_gemv_w8a16 with flags (same reference counterpart).  M <= 256 with
+   16-byte aligned rows runs on the tensor cores (swap-AB, split-K over a
+   thread-block cluster); other shapes on CUDA cores. */
+int hx_gemv_w8a16_ex(int64_t M, int64_t N, int64_t K, const void *x,
+                     int64_t ldx, const int8_t *W, int64_t ldw,
+                     const void *scale, const void *bias, void *y,
+                     int64_t ldy, int flags, void *stream);
+
+/* One projection of a grouped W8A16 launch: y[M,N] = x[M,K] . (W[N,K] *
+   scale[N])^T (+ bias[N]); all f16 except W (s8).  `dep` names an earlier
+   projection of the same launch whose y is this projection's x (the launch
+   orders them), or -1.  No y may alias another projection's x or y except
+   through such a dependency. */
+typedef struct hx_w8a16_proj {
+  int64_t N, K;
+  const void *x;
+  int64_t ldx;
+  const int8_t *W;
+  int64_t ldw;
+  const void *scale;
+  const void *bias;
+  void *y;
+  int64_t ldy;
+  int32_t dep;
+  int32_t reserved;
+} hx_w8a16_proj;
+
+/* Run up to 256 W8A16 projections (a decode step's linears) in one
+   persistent launch, M <= 8, K % 16 == 0, 16-byte aligned rows.  Weight rows
+   stream into shared memory ahead of use; dependent projections wait on
+   per-projection completion counters.  `counters` is caller-owned device
+   scratch of `count` int32, zeroed by this call (cudaMemsetAsync on the
+   stream).  Same per-projection arithmetic as hx_gemv_w8a16 (reference:
+   dequantise + matmul, LinalgToLLVMPass.cpp:203-209); the grouping itself
+   has no reference counterpart. */
+int hx_gemv_w8a16_grouped(int64_t M, int count, const hx_w8a16_proj *projs,
+                          int32_t *counters, int32_t *error_flag, void *stream);
+
 /* Column-sharded GEMM followed by an all-gather of the output over NCCL.
    Rank r holds its shard of the weight, B rows [r*Ns, (r+1)*Ns) (HX_B_NK),
    with Ns = d->N, and computes C_r = epilogue(A . B_r^T) into d->C

@@ -220,19 +220,54 @@ def test_int8_dequant_epilogue(cuda_device):
 
 
 # ---------------------------------------------------------------- W8A16
+@pytest.mark.parametrize("path", ["auto", "auto_const", "cuda_core"])
 @pytest.mark.parametrize("M", [1, 2, 3, 8, 32, 64])
 @pytest.mark.parametrize("NK", [(2048, 2048), (256, 2048), (5632, 2048), (2048, 5632)],
                          ids=lambda s: f"{s[0]}x{s[1]}")
-def test_w8a16(cuda_device, M, NK):
+def test_w8a16(cuda_device, M, NK, path):
     q = hx()
     N, K = NK
     g = torch.Generator().manual_seed(13 + M)
     w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int64).to(torch.int8)
     scale = (torch.rand(N, generator=g) * 0.019 + 0.001).half()
     x = torch.randn(M, K, generator=g).half()
-    y = q.gemv_w8a16(x.cuda(), w.cuda(), scale.cuda())
+    y = q.gemv_w8a16(x.cuda(), w.cuda(), scale.cuda(), weights_const=(path == "auto_const"),
+                     force_cuda_core=(path == "cuda_core"))
     torch.cuda.synchronize()
     assert_close(to_np32(y), O.w8a16_ref(x.numpy(), w.numpy(), scale.numpy()))
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 300, 1000), (256, 384, 512), (100, 129, 2064), (5, 7, 48)])
+def test_w8a16_tc_odd_shapes(cuda_device, M, N, K):
+    """Batch up to 256 (MPAD 128/256), N and K tails, bias."""
+    q = hx()
+    g = torch.Generator().manual_seed(M + N + K)
+    w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int64).to(torch.int8)
+    scale = (torch.rand(N, generator=g) * 0.019 + 0.001).half()
+    bias = (torch.randn(N, generator=g) * 0.02).half()
+    x = torch.randn(M, K, generator=g).half()
+    y = q.gemv_w8a16(x.cuda(), w.cuda(), scale.cuda(), bias=bias.cuda())
+    torch.cuda.synchronize()
+    assert_close(to_np32(y), O.w8a16_ref(x.numpy(), w.numpy(), scale.numpy(), bias.numpy()))
+
+
+def test_w8a16_back_to_back_const(cuda_device):
+    """Chained decode projections with the constant-weight prefetch: the
+    second call reads the first call's output."""
+    q = hx()
+    g = torch.Generator().manual_seed(21)
+    w1 = torch.randint(-127, 128, (2048, 2048), generator=g, dtype=torch.int64).to(torch.int8)
+    w2 = torch.randint(-127, 128, (512, 2048), generator=g, dtype=torch.int64).to(torch.int8)
+    s1 = (torch.rand(2048, generator=g) * 0.001 + 0.0005).half()
+    s2 = (torch.rand(512, generator=g) * 0.019 + 0.001).half()
+    x = torch.randn(8, 2048, generator=g).half()
+    d = cuda_device
+    for _ in range(3):
+        h = q.gemv_w8a16(x.to(d), w1.to(d), s1.to(d), weights_const=True)
+        y = q.gemv_w8a16(h, w2.to(d), s2.to(d), weights_const=True)
+    torch.cuda.synchronize()
+    h_ref = O.w8a16_ref(x.numpy(), w1.numpy(), s1.numpy()).astype(np.float16)
+    assert_close(to_np32(y), O.w8a16_ref(h_ref, w2.numpy(), s2.numpy()))
 
 
 def test_w8a16_unaligned_scalar(cuda_device):
@@ -290,3 +325,42 @@ def test_cpu_tensor_rejected(cuda_device):
     q = hx()
     with pytest.raises(ValueError):
         q.gemm(torch.randn(4, 4).half(), torch.randn(4, 4).half())
+
+
+# ---------------------------------------------------------------- grouped W8A16
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_w8a16_grouped_chain(cuda_device, M):
+    """A decode-layer-like list in one launch: independent projections plus a
+    dependent chain (q -> o, gate -> down), checked against the oracle."""
+    q = hx()
+    d = cuda_device
+    g = torch.Generator().manual_seed(30 + M)
+
+    def wq(n, k, s_hi=0.02):
+        w = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int64).to(torch.int8)
+        s = (torch.rand(n, generator=g) * (s_hi - 0.001) + 0.001).half()
+        return w, s
+
+    x = torch.randn(M, 2048, generator=g).half()
+    shapes = [(2048, 2048, -1, 0.0015), (256, 2048, -1, 0.02), (5632, 2048, -1, 0.0015),
+              (2048, 2048, 0, 0.02), (2048, 5632, 2, 0.02), (100, 48, -1, 0.02)]
+    grp = q.ops.W8A16Group(M, d)
+    ys, ws = [], []
+    for i, (n, k, dep, shi) in enumerate(shapes):
+        w, s = wq(n, k, shi)
+        ws.append((w, s))
+        xin = ys[dep] if dep >= 0 else (x.to(d) if k == 2048 else torch.randn(M, k, generator=g).half().to(d))
+        y = torch.empty(M, n, dtype=torch.float16, device=d)
+        ys.append(y)
+        grp.add(xin, w.to(d), s.to(d), y, dep=dep)
+        ws[-1] = (w, s, xin)
+    for _ in range(2):  # run twice: counters are reset per launch
+        grp.run()
+    torch.cuda.synchronize()
+    assert int(grp.error_flag.item()) == 0
+    refs = []
+    for i, (n, k, dep, _) in enumerate(shapes):
+        w, s, xin = ws[i]
+        xr = refs[dep].astype(np.float16) if dep >= 0 else to_np32(xin)
+        refs.append(O.w8a16_ref(xr, w.numpy(), s.numpy()))
+        assert_close(to_np32(ys[i]), refs[-1])
