@@ -801,6 +801,59 @@ int hx_gemv_w8a16_grouped(int64_t M, int count, const hx_w8a16_proj *projs, int3
                                static_cast<cudaStream_t>(stream));
 }
 
+}  // extern "C"
+
+// ------------------------------------------------------------ allocation-free grouped W8A16
+// Completion counters for hx_gemv_w8a16_grouped_noalloc, one int32 per
+// projection, in a fixed device array that every GPU loading this library
+// holds until the process exits (1 KB).  In host code `g_noalloc_counters`
+// names a host-side stand-in, not device memory: its device address is
+// looked up per device with cudaGetSymbolAddress below.
+#define HX_NOALLOC_MAX_PROJS 256
+static __device__ __align__(256) int32_t g_noalloc_counters[HX_NOALLOC_MAX_PROJS];
+
+namespace hx {
+namespace {
+std::mutex g_noalloc_mu;
+int32_t *g_noalloc_ptr[64] = {};  // device address of the array, per device
+
+// Set-up, once per device, with that device current.
+int noalloc_counters(int32_t **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return arg_fail("device index out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void *ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_counters);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_counters)");
+    g_noalloc_ptr[dev] = static_cast<int32_t *>(ptr);
+  }
+  *out = g_noalloc_ptr[dev];
+  return HX_OK;
+}
+}  // namespace
+}  // namespace hx
+
+extern "C" {
+
+int hx_gemv_w8a16_grouped_noalloc(int64_t M, int count, const hx_w8a16_proj *projs,
+                                  int32_t *error_flag, void *stream) {
+  hx::g_last_error.clear();
+  if (count > HX_NOALLOC_MAX_PROJS) {
+    hx::g_last_error = "hx_gemv_w8a16_grouped_noalloc takes at most 256 projections";
+    return HX_E_TOO_LARGE;
+  }
+  int32_t *counters = nullptr;
+  const int rc = hx::noalloc_counters(&counters);
+  if (rc != HX_OK) return rc;
+  // gemv_grouped_impl zeroes the counters with cudaMemsetAsync on `stream`
+  // before the launch; it allocates nothing.
+  return hx::gemv_grouped_impl(M, count, projs, counters, error_flag,
+                               static_cast<cudaStream_t>(stream));
+}
+
 int hx_query_workspace(const hx_gemm_desc *d, int64_t *bytes) {
   if (!d || !bytes) return HX_E_INVALID_ARG;
   *bytes = 0;

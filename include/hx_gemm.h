@@ -175,6 +175,26 @@ typedef struct hx_w8a16_proj {
 int hx_gemv_w8a16_grouped(int64_t M, int count, const hx_w8a16_proj *projs,
                           int32_t *counters, int32_t *error_flag, void *stream);
 
+/* Same as hx_gemv_w8a16_grouped, for callers that cannot allocate device
+   memory: no counters argument, and no cudaMalloc/cudaFree or allocating
+   library call anywhere in it.  Such callers include serving engines whose
+   memory pool owns the whole GPU from start-up, latency-critical decode loops
+   where an allocation could synchronise the device, and hosts that reach
+   this library through a foreign-function interface and only hand it
+   pointers they already own.  The per-projection counters live instead in
+   a fixed device array of this library (256 int32 = 1 KB per GPU, kept until
+   the process exits), so `count` may be at most 256; larger counts return
+   HX_E_TOO_LARGE.  The first call on each device looks up that array's
+   device address (with the device current), so make the first call before
+   any stream capture.  Each call zeroes the counters on `stream` before its
+   launch; all calls share the one array, so calls that can overlap on the
+   GPU (different streams, or the same array used from several threads at
+   once) race and must be serialised by the caller.  This entry point has no
+   counterpart in the reference. */
+int hx_gemv_w8a16_grouped_noalloc(int64_t M, int count,
+                                  const hx_w8a16_proj *projs,
+                                  int32_t *error_flag, void *stream);
+
 /* Column-sharded GEMM followed by an all-gather of the output over NCCL.
    Rank r holds its shard of the weight, B rows [r*Ns, (r+1)*Ns) (HX_B_NK),
    with Ns = d->N, and computes C_r = epilogue(A . B_r^T) into d->C
