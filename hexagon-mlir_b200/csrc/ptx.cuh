@@ -63,7 +63,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
 }
 // 2-D tiled bulk tensor load global -> shared, completing on `bar`.
 // x = innermost (contiguous) coordinate in elements, y = row.
-// No cluster multicast: each CTA loads its own tiles.
+// Each CTA loads its own tiles; loads are never shared across CTAs.
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, uint64_t *bar,
                                             int32_t x, int32_t y) {
   asm volatile(

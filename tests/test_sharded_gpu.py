@@ -1,0 +1,79 @@
+"""Multi-GPU parity of the column-sharded GEMM (BASELINE config 5 shape,
+scaled down): every rank computes its column shard with hx kernels and the
+full logits are assembled (a) with torch.distributed NCCL all-gather and (b)
+with the library's own NCCL communicator (hx_sharded_gemm_allgather).
+Needs >= 2 GPUs; runs as child processes, one per GPU."""
+
+import os
+import socket
+import subprocess
+import sys
+import textwrap
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+WORKER = textwrap.dedent(r'''
+    import os, sys
+    sys.path.insert(0, os.path.join(ROOT, "hexagon-mlir_b200")); sys.path.insert(0, ROOT)
+    import numpy as np, torch, torch.distributed as dist
+    from qcom_hexagon_backend import sharding as S
+    from oracle import gemm_oracle as O
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
+    M, K, N = 512, 256, 1000
+    g = torch.Generator().manual_seed(9)
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    ref = O.matmul_f32(a.float().numpy(), w.float().numpy())
+    lin = S.ColumnShardedLinear(w.cuda(), N, rank, world, full=True)
+    y1 = lin.forward(a.cuda()).float().cpu().numpy()
+    comm = S.NcclComm()
+    lin2 = S.ColumnShardedLinear(w.cuda(), N, rank, world, full=True, comm=comm)
+    y2 = lin2.forward(a.cuda()).float().cpu().numpy()
+    local = lin.forward(a.cuda(), gather=False).float().cpu().numpy()
+    n0, n1 = S.shard_range(N, world, rank)
+    e1, e2 = O.max_rel_err(y1, ref), O.max_rel_err(y2, ref)
+    e3 = O.max_rel_err(local[:, : n1 - n0], ref[:, n0:n1])
+    assert y1.shape == (M, N) and y2.shape == (M, N), (y1.shape, y2.shape)
+    assert e1 <= 1e-2 and e2 <= 1e-2 and e3 <= 1e-2, (e1, e2, e3)
+    torch.cuda.synchronize(); comm.close(); dist.destroy_process_group()
+    print("rank", rank, "ok", e1, e2, e3)
+''')
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_sharded_lmhead_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    port = _port()
+    env = dict(os.environ, MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world),
+               NCCL_NVLS_ENABLE="0")
+    code = f"ROOT = {ROOT!r}\n" + WORKER
+    procs = [subprocess.Popen([sys.executable, "-c", code], env=dict(env, RANK=str(r)),
+                              stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+             for r in range(world)]
+    outs = []
+    for p in procs:
+        try:
+            out, _ = p.communicate(timeout=240)
+        except subprocess.TimeoutExpired:
+            p.kill()
+            out, _ = p.communicate()
+        outs.append(out)
+    for r, (p, out) in enumerate(zip(procs, outs)):
+        assert p.returncode == 0, f"rank {r} failed:\n{out[-3000:]}"
+        assert f"rank {r} ok" in out
