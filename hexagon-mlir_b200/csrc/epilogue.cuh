@@ -57,13 +57,16 @@ __device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.f + __ex
 
 // Load 32 consecutive elements v[j] = p[n0 + j] as float, j < 32 (columns
 // >= N read as 0).  `vec_ok`: p is 16-byte aligned (n0 is a multiple of 32).
+// COHERENT: read through L2 only (data another CTA of the same launch may
+// have written); otherwise the read-only path.
+template <bool COHERENT = false>
 __device__ __forceinline__ void load_row32(const void *p, int dtype, int64_t base, int n0, int N,
                                            bool vec_ok, float (&v)[32]) {
   if (vec_ok && n0 + 32 <= N && (dtype == HX_F16 || dtype == HX_BF16)) {
     const uint4 *q = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(p) + base + n0);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint4 w = __ldg(q + i);
+      const uint4 w = COHERENT ? __ldcg(q + i) : __ldg(q + i);
       const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
@@ -84,7 +87,7 @@ __device__ __forceinline__ void load_row32(const void *p, int dtype, int64_t bas
     const float4 *q = reinterpret_cast<const float4 *>(static_cast<const float *>(p) + base + n0);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float4 w = __ldg(q + i);
+      const float4 w = COHERENT ? __ldcg(q + i) : __ldg(q + i);
       v[4 * i] = w.x;
       v[4 * i + 1] = w.y;
       v[4 * i + 2] = w.z;
@@ -122,7 +125,7 @@ __device__ __forceinline__ void epi_transform32(const EpiArgs &e, float (&v)[32]
     for (int j = 0; j < 32; ++j) v[j] += t[j];
   }
   if ((epi == HX_EPI_BIAS_RESIDUAL || epi == HX_EPI_RESIDUAL) && m < e.M) {
-    load_row32(e.residual, e.c_dtype, static_cast<int64_t>(m) * e.ldr, n0, e.N, e.r_vec_ok, t);
+    load_row32<true>(e.residual, e.c_dtype, static_cast<int64_t>(m) * e.ldr, n0, e.N, e.r_vec_ok, t);
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] += t[j];
   }

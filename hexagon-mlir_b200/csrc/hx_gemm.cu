@@ -19,6 +19,7 @@
 #include <string>
 #include <utility>
 
+#include "gemm_chain.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_sm100.cuh"
 #include "gemv_grouped.cuh"
@@ -578,6 +579,96 @@ int gemv_impl(int64_t M, int64_t N, int64_t K, const void *x, int64_t ldx, const
   return HX_OK;
 }
 
+// ------------------------------------------------------------ GEMM chain
+static_assert(sizeof(ChainParams) < 32000, "chain parameter block must fit the launch limit");
+
+int gemm_chain_impl(const hx_gemm_desc *descs, const int32_t *a_dep, const int32_t *r_dep,
+                    int count, int32_t *counters, int64_t counters_len, int32_t *error_flag,
+                    cudaStream_t s) {
+  if (count < 0) return arg_fail("negative count");
+  if (count == 0) return HX_OK;
+  if (count > kChainMax) {
+    g_last_error = "hx_gemm_chain takes at most 64 GEMMs per call";
+    return HX_E_TOO_LARGE;
+  }
+  if (!descs || !a_dep || !r_dep || !counters) return arg_fail("null argument");
+  int sms = 0, major = 0;
+  int rc = current_device_info(&sms, &major);
+  if (rc != HX_OK) return rc;
+  if (major != 10) {
+    g_last_error = "current device is not sm_100";
+    return HX_E_NO_DEVICE;
+  }
+  constexpr int BN = 128;
+  static ChainParams p;  // ~26 KB, passed by value at launch
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  int64_t tiles = 0, ctrs = 0;
+  for (int g = 0; g < count; ++g) {
+    const hx_gemm_desc *d = &descs[g];
+    rc = validate(d);
+    if (rc != HX_OK) return rc;
+    if (d->M == 0 || d->N == 0 || d->K == 0) return unsupported("empty GEMM in a chain");
+    if (d->a_dtype != HX_F16 && d->a_dtype != HX_BF16) return unsupported("chain takes f16/bf16");
+    if (d->b_layout != HX_B_NK) return unsupported("chain takes the W[N,K] layout");
+    if (d->epilogue == HX_EPI_DEQUANT_SCALE) return unsupported("chain epilogue");
+    if (!aligned16(d->A) || !aligned16(d->B) || (d->lda * 2) % 16 || (d->ldb * 2) % 16)
+      return unsupported("chain operands need 16-byte aligned rows");
+    for (const int32_t dep : {a_dep[g], r_dep[g]}) {
+      if (dep < -1 || dep >= g) return arg_fail("dependencies must name earlier GEMMs");
+      if (dep >= 0 && descs[dep].M != d->M) return arg_fail("a dependency must have the same M");
+    }
+    if (r_dep[g] >= 0 && !d->residual) return arg_fail("r_dep without a residual");
+    const bool sw = d->epilogue == HX_EPI_SWIGLU;
+    ChainGemm &c = p.g[g];
+    c.m_tiles = static_cast<int32_t>((d->M + kBM - 1) / kBM);
+    const int out_w = sw ? BN / 2 : BN;
+    c.n_tiles = static_cast<int32_t>((d->N + out_w - 1) / out_w);
+    c.k_blocks = static_cast<int32_t>((d->K + 63) / 64);
+    c.n_half = static_cast<int32_t>(d->N);
+    c.swiglu = sw ? 1 : 0;
+    c.a_dep = a_dep[g];
+    c.r_dep = r_dep[g];
+    c.tile_begin = static_cast<int32_t>(tiles);
+    c.ctr_begin = static_cast<int32_t>(ctrs);
+    c.idesc = make_idesc(d->a_dtype == HX_F16 ? 0 : 1, false, kBM, BN);
+    c.epi = make_epi(d);
+    rc = make_tmap(&p.tma[g], d->A, d->a_dtype, d->K, d->M, d->lda, 64, kBM);
+    if (rc != HX_OK) return rc;
+    rc = make_tmap(&p.tmb[g], d->B, d->b_dtype, d->K, sw ? 2 * d->N : d->N, d->ldb, 64,
+                   sw ? BN / 2 : BN);
+    if (rc != HX_OK) return rc;
+    tiles += static_cast<int64_t>(c.m_tiles) * c.n_tiles;
+    ctrs += c.m_tiles;
+    if (tiles > INT32_MAX) return unsupported("too many tiles");
+  }
+  if (counters_len < ctrs) {
+    g_last_error = "counters buffer too small: needs one int32 per 128-row block of every GEMM";
+    return HX_E_INVALID_ARG;
+  }
+  p.count = count;
+  p.total_tiles = static_cast<int32_t>(tiles);
+  p.stages = std::min(8, (kMaxDynSmem - 1280) / stage_bytes(BN));
+  p.counters = counters;
+  p.err_flag = error_flag;
+  p.timeout = kDefaultTimeout;
+  cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int32_t) * ctrs, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(chain counters)");
+  auto kern = hx_gemm_chain_kernel<BN>;
+  const int smem = p.stages * stage_bytes(BN) + 1024 + 256;
+  static std::atomic<int> configured{0};
+  if (!configured.load(std::memory_order_acquire)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(chain)");
+    configured.store(1, std::memory_order_release);
+  }
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
+  e = launch_pdl(kern, dim3(grid), dim3(kThreads), static_cast<size_t>(smem), s, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "hx_gemm_chain_kernel launch");
+  return HX_OK;
+}
+
 // ------------------------------------------------------------ grouped W8A16
 int gemv_grouped_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32_t *counters,
                       int32_t *error_flag, cudaStream_t s) {
@@ -792,6 +883,13 @@ int hx_gemv_w8a16_ex(int64_t M, int64_t N, int64_t K, const void *x, int64_t ldx
   if (flags & ~(HX_GEMV_WEIGHTS_CONST | HX_GEMV_FORCE_CUDA_CORE)) return HX_E_INVALID_ARG;
   return hx::gemv_impl(M, N, K, x, ldx, W, ldw, scale, bias, y, ldy, flags,
                        static_cast<cudaStream_t>(stream));
+}
+
+int hx_gemm_chain(const hx_gemm_desc *descs, const int32_t *a_dep, const int32_t *r_dep, int count,
+                  int32_t *counters, int64_t counters_len, int32_t *error_flag, void *stream) {
+  hx::g_last_error.clear();
+  return hx::gemm_chain_impl(descs, a_dep, r_dep, count, counters, counters_len, error_flag,
+                             static_cast<cudaStream_t>(stream));
 }
 
 int hx_gemv_w8a16_grouped(int64_t M, int count, const hx_w8a16_proj *projs, int32_t *counters,

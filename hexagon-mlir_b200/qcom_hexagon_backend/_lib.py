@@ -112,6 +112,7 @@ SIGNATURES = {
     "hx_gemv_w8a16_ex": (_I32, [_I64, _I64, _I64, _VP, _I64, _VP, _I64, _VP, _VP, _VP, _I64, _I32, _VP]),
     "hx_gemv_w8a16_grouped": (_I32, [_I64, _I32, ctypes.POINTER(HxW8A16Proj), _VP, _VP, _VP]),
     "hx_gemv_w8a16_grouped_noalloc": (_I32, [_I64, _I32, ctypes.POINTER(HxW8A16Proj), _VP, _VP]),
+    "hx_gemm_chain": (_I32, [ctypes.POINTER(HxGemmDesc), _VP, _VP, _I32, _VP, _I64, _VP, _VP]),
     "hx_sharded_gemm_allgather": (_I32, [ctypes.POINTER(HxGemmDesc), _I32, _I32, _VP, _VP, _VP]),
     "hx_shards_to_rows": (_I32, [_VP, _VP, _I32, _I64, _I64, _I32, _VP]),
     "hx_nccl_unique_id_size": (_I32, []),

@@ -84,6 +84,7 @@ class HexagonOptions:
     device: int = 0                 # CUDA device index
     fuse_epilogue: bool = True      # fold bias/GELU/SiLU/SwiGLU/residual into the GEMM
     use_cuda_graph: bool = True     # capture the compiled graph's launches once, replay
+    chain_gemms: bool = False       # run consecutive linears as one persistent launch
     world_size: int = 1             # column-sharding degree (LM-head style GEMMs)
     shard_dim: str = "n"            # only "n" (output columns) is supported
 

@@ -23,6 +23,7 @@ Everything else in the graph runs unchanged (on the GPU, as torch ops).
 
 from __future__ import annotations
 
+import copy
 import operator
 from typing import Callable, Optional
 
@@ -46,7 +47,9 @@ def hx_linear(x, weight, bias=None, residual=None, activation=None):
         out_shape = (*x.shape[:-1], weight.shape[0])
         if tuple(residual.shape) != out_shape or residual.dtype != x.dtype:
             # Broadcasting residual: not an epilogue the kernel fuses.
-            return ops.linear(x, weight, bias, activation=activation) + residual
+            y = ops.linear(x, weight, bias, activation=activation)
+            ops.chain_flush()  # the add below reads y
+            return y + residual
     return ops.linear(x, weight, bias, activation=activation, residual=residual)
 
 
@@ -179,6 +182,24 @@ def rewrite(gm: fx.GraphModule) -> fx.GraphModule:
     return gm
 
 
+def insert_chain_flushes(gm: fx.GraphModule) -> fx.GraphModule:
+    """Before every node that may read tensor data and is not a fused linear,
+    insert ops.chain_flush(), so GEMMs queued by ops.chained() have run.
+    Fused linears queue themselves; getitem (views) reads nothing."""
+    graph = gm.graph
+    for n in list(graph.nodes):
+        if n.op in ("placeholder", "get_attr"):
+            continue
+        if n.op == "call_function" and (n.target in (hx_linear, hx_swiglu, ops.chain_flush)
+                                        or n.target is operator.getitem):
+            continue
+        with graph.inserting_before(n):
+            graph.call_function(ops.chain_flush, ())
+    graph.lint()
+    gm.recompile()
+    return gm
+
+
 def _has_param(gm, qualname):
     try:
         gm.get_parameter(qualname)
@@ -191,12 +212,16 @@ def count_hx_calls(gm: fx.GraphModule) -> int:
     return sum(1 for n in gm.graph.nodes if n.op == "call_function" and n.target in (hx_linear, hx_swiglu))
 
 
-def compile_module(module: nn.Module, device: torch.device | str = "cuda") -> fx.GraphModule:
+def compile_module(module: nn.Module, device: torch.device | str = "cuda",
+                   chain: bool = False) -> fx.GraphModule:
     """Trace `module`, move its parameters to `device` and rewrite its linear
-    layers onto the B200 kernels.  The original module is not modified."""
-    gm = fx.symbolic_trace(module)
+    layers onto the B200 kernels.  With `chain`, flush points are inserted so
+    the graph can run under ops.chained() (consecutive linears become one
+    hx_gemm_chain launch).  The original module is not modified."""
+    gm = fx.symbolic_trace(copy.deepcopy(module))  # the GraphModule would share parameters
     gm = gm.to(device)
-    return rewrite(gm)
+    gm = rewrite(gm)
+    return insert_chain_flushes(gm) if chain else gm
 
 
 def hexagon_backend(gm: fx.GraphModule, example_inputs) -> Callable:

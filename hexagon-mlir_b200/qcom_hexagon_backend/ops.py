@@ -88,11 +88,125 @@ def gemm(
                             bias=bias, residual=residual, scale=scale, tile_n=tile_n, stages=stages,
                             max_ctas=max_ctas, force_simt=force_simt, error_flag=error_flag,
                             timeout_cycles=timeout_cycles)
+    rec = _recorder
+    if rec is not None and rec.device == dev:
+        if rec.accepts(d, a, b, residual, b_layout, tile_n, stages, max_ctas, force_simt):
+            rec.add(d, a, b, out, residual, bias, scale)
+            return out
+        rec.flush()
     lib = _lib.load()
     with torch.cuda.device(dev):
         rc = lib.hx_gemm(ctypes.byref(d), ctypes.c_void_p(_stream_ptr(dev)))
     _lib.check(rc, "hx_gemm")
     return out
+
+
+class ChainRecorder:
+    """Collects consecutive fused GEMMs and runs them as one hx_gemm_chain
+    launch, so consecutive linear layers overlap on the GPU.
+
+    Inside `with ops.chained():` every eligible gemm()/linear() call returns
+    its (not yet computed) output and is queued; its A operand and residual
+    are matched against queued outputs (views such as a column slice count)
+    to find the dependencies.  flush() launches the queue; it runs when the
+    scope ends, before an ineligible call, and wherever the caller reads the
+    data (fx_backend inserts ops.chain_flush before every node that is not a
+    fused linear or a view).
+    """
+
+    MAX = 64
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self.descs, self.a_dep, self.r_dep, self.outs, self.keep = [], [], [], [], []
+
+    def _producer(self, t):
+        if t is None:
+            return -1
+        p = t.data_ptr()
+        for i in range(len(self.outs) - 1, -1, -1):
+            o = self.outs[i]
+            lo = o.data_ptr()
+            if lo <= p < lo + o.numel() * o.element_size():
+                return i
+        return -1
+
+    def accepts(self, d, a, b, residual, b_layout, tile_n, stages, max_ctas, force_simt):
+        if b_layout != "nk" or tile_n or stages or max_ctas or force_simt:
+            return False
+        if a.dtype not in (torch.float16, torch.bfloat16) or d.K == 0 or d.M == 0 or d.N == 0:
+            return False
+        if d.epilogue == _lib.HX_EPI_DEQUANT_SCALE:
+            return False
+        if a.data_ptr() % 16 or b.data_ptr() % 16 or (d.lda * 2) % 16 or (d.ldb * 2) % 16:
+            return False
+        for t in (a, residual):
+            i = self._producer(t)
+            if i >= 0 and self.descs[i].M != d.M:
+                return False
+        return True
+
+    def add(self, d, a, b, out, residual, bias, scale):
+        if len(self.descs) == self.MAX:
+            self.flush()
+        self.a_dep.append(self._producer(a))
+        self.r_dep.append(self._producer(residual))
+        self.descs.append(d)
+        self.outs.append(out)
+        self.keep.append((a, b, residual, bias, scale))
+
+    def flush(self):
+        n = len(self.descs)
+        if n == 0:
+            return
+        arr = (_lib.HxGemmDesc * n)(*self.descs)
+        ad = (ctypes.c_int32 * n)(*self.a_dep)
+        rd = (ctypes.c_int32 * n)(*self.r_dep)
+        nctr = sum((d.M + 127) // 128 for d in self.descs)
+        counters = torch.empty(nctr, dtype=torch.int32, device=self.device)
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            rc = lib.hx_gemm_chain(arr, ad, rd, n, ctypes.c_void_p(counters.data_ptr()), nctr, None,
+                                   ctypes.c_void_p(_stream_ptr(self.device)))
+        self.keep.append(counters)
+        keep = self.keep
+        self.descs, self.a_dep, self.r_dep, self.outs, self.keep = [], [], [], [], []
+        _lib.check(rc, "hx_gemm_chain")
+        # Operands may be freed now: any reuse of their memory is stream-ordered
+        # after this launch.
+        del keep
+
+
+_recorder: Optional[ChainRecorder] = None
+
+
+class chained:
+    """Context manager: queue eligible GEMMs and run them as hx_gemm_chain launches."""
+
+    def __init__(self, device):
+        self.device = device
+
+    def __enter__(self):
+        global _recorder
+        if _recorder is not None:
+            raise RuntimeError("ops.chained() does not nest")
+        _recorder = ChainRecorder(self.device)
+        return _recorder
+
+    def __exit__(self, *exc):
+        global _recorder
+        rec, _recorder = _recorder, None
+        if exc[0] is None:
+            rec.flush()
+        return False
+
+
+def chain_flush(*args):
+    """Run any queued chained GEMMs (a no-op outside ops.chained()); returns
+    its first argument so it can sit in an FX graph before a data read."""
+    if _recorder is not None:
+        _recorder.flush()
+    return args[0] if args else None
 
 
 def make_desc(a, b, *, b_layout="nk", out=None, out_dtype=None, epilogue="none", bias=None,

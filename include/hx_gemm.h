@@ -112,6 +112,22 @@ typedef struct hx_gemm_desc {
    _mlir_ciface_<fn> entry of the generated .so. */
 int hx_gemm(const hx_gemm_desc *d, void *stream);
 
+/* A list of fused GEMMs (a stack of linear layers) as one persistent launch.
+   GEMM g may read as A (a_dep[g] >= 0) and/or as its residual (r_dep[g] >= 0)
+   the C of an earlier GEMM of the list with the same M; a tile of row block
+   m of GEMM g starts as soon as row block m of those producers is complete,
+   so consecutive layers overlap instead of running back to back.  f16/bf16,
+   W[N,K] layout, 16-byte aligned rows, any epilogue but DEQUANT_SCALE, at
+   most 64 GEMMs (HX_E_TOO_LARGE beyond).  `counters` is caller-owned device
+   scratch of counters_len int32, at least one per 128-row block of every
+   GEMM; this call zeroes them on `stream`.  Output buffers must not alias
+   any other GEMM's inputs or outputs of the list.  Replaces the sequence of
+   linalg.matmul + linalg.generic ops the reference compiles and runs one by
+   one (lib/Conversion/LinalgToLLVM/LinalgToLLVMPass.cpp:188-400). */
+int hx_gemm_chain(const hx_gemm_desc *descs, const int32_t *a_dep,
+                  const int32_t *r_dep, int count, int32_t *counters,
+                  int64_t counters_len, int32_t *error_flag, void *stream);
+
 /* HexKL drop-in: out[n_row, n_col] (f32) = act[n_row, n_inner] (f16) .
    W[n_inner, n_col] (f16), fp32 accumulate.  Replaces
    hexkl_matmul_f16f16_f32 (bin/runtime/src/HexKLAPI.cpp:15-17); unlike
