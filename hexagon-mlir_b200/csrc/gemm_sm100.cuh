@@ -46,6 +46,9 @@ struct GemmParams {
   int32_t group_m;                // grouped raster: m-tiles per group
   int32_t total_tiles;
   int32_t stages;                 // depth of the smem ring
+  int32_t kbs;                    // 128-byte K blocks per stage (one TMA load each for A, B)
+  int32_t stage_blocks;           // stages per tile: ceil(k_blocks / kbs)
+  int32_t use3d;                  // 3-D maps (K blocks as the third dimension)
   uint64_t timeout;               // cycles per bounded wait
   int32_t *err_flag;              // optional global error word
   EpiArgs epi;
@@ -64,6 +67,7 @@ struct GemmCfg {
   static constexpr int kMNChunk = kKBytes / kElem;                // MN elems per 128 B
   static constexpr int smem_bytes(int stages) { return stages * kStageBytes + 1024 /*align*/ + 256 /*bars*/; }
   static constexpr uint32_t kIdesc = make_idesc(KIND, B_MN, kBM, BN);
+  static constexpr uint32_t kIdescHalf = make_idesc(KIND, B_MN, kBM, BN / 2);  // SWIGLU halves
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
   static_assert(!(SWIGLU && B_MN), "SWIGLU needs the W[N,K] layout");
   static_assert(kTmemCols >= 32 && kTmemCols <= 512, "TMEM columns");
@@ -95,9 +99,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   // 1024-byte alignment for the 128B-swizzle atoms.
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int A_ST = p.kbs * Cfg::kABytes;  // bytes of A per stage
+  const int B_ST = p.kbs * Cfg::kBBytes;  // bytes of B per stage
   uint8_t *sA = smem;
-  uint8_t *sB = smem + STAGES * Cfg::kABytes;
-  uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + STAGES * Cfg::kStageBytes);
+  uint8_t *sB = smem + STAGES * A_ST;
+  uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + STAGES * (A_ST + B_ST));
   uint64_t *empty_bar = full_bar + STAGES;
   uint64_t *tfull_bar = empty_bar + STAGES;   // [2]
   uint64_t *tempty_bar = tfull_bar + 2;       // [2]
@@ -148,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int m_blk, n_blk;
       tile_coords(t, p, m_blk, n_blk);
       const int m0 = m_blk * kBM;
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
+      for (int sb = 0; sb < p.stage_blocks; ++sb) {
         bool w = (lane == 0) ? mbar_wait(&empty_bar[stage], phase ^ 1, p.timeout, abort_flag)
                              : true;
         w = __shfl_sync(0xffffffffu, w, 0);
@@ -159,21 +165,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (lane == 0) {
           uint64_t *fb = &full_bar[stage];
-          mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
-          const int kx = kb * Cfg::kBKElems;
-          tma_load_2d(sA + stage * Cfg::kABytes, &tmA, fb, kx, m0);
-          uint8_t *dstB = sB + stage * Cfg::kBBytes;
-          if constexpr (B_MN) {
+          mbar_arrive_expect_tx(fb, A_ST + B_ST);
+          uint8_t *dstA = sA + stage * A_ST;
+          uint8_t *dstB = sB + stage * B_ST;
+          if constexpr (B_MN) {  // kbs == 1, 2-D maps
+            const int kx = sb * Cfg::kBKElems;
+            tma_load_2d(dstA, &tmA, fb, kx, m0);
             const int n0 = n_blk * BN;
 #pragma unroll
             for (int j = 0; j < BN / Cfg::kMNChunk; ++j)
               tma_load_2d(dstB + j * (Cfg::kBKElems * 128), &tmB, fb, n0 + j * Cfg::kMNChunk, kx);
-          } else if constexpr (SWIGLU) {
-            const int n0 = n_blk * (BN / 2);
-            tma_load_2d(dstB, &tmB, fb, kx, n0);
-            tma_load_2d(dstB + (BN / 2) * kKBytes, &tmB, fb, kx, p.n_half + n0);
-          } else {
-            tma_load_2d(dstB, &tmB, fb, kx, n_blk * BN);
+          } else if (p.use3d) {
+            const int kz = sb * p.kbs;
+            tma_load_3d(dstA, &tmA, fb, 0, m0, kz);
+            if constexpr (SWIGLU) {
+              const int n0 = n_blk * (BN / 2);
+              tma_load_3d(dstB, &tmB, fb, 0, n0, kz);
+              tma_load_3d(dstB + B_ST / 2, &tmB, fb, 0, p.n_half + n0, kz);
+            } else {
+              tma_load_3d(dstB, &tmB, fb, 0, n_blk * BN, kz);
+            }
+          } else {  // kbs == 1, 2-D maps
+            const int kx = sb * Cfg::kBKElems;
+            tma_load_2d(dstA, &tmA, fb, kx, m0);
+            if constexpr (SWIGLU) {
+              const int n0 = n_blk * (BN / 2);
+              tma_load_2d(dstB, &tmB, fb, kx, n0);
+              tma_load_2d(dstB + B_ST / 2, &tmB, fb, kx, p.n_half + n0);
+            } else {
+              tma_load_2d(dstB, &tmB, fb, kx, n_blk * BN);
+            }
           }
         }
         __syncwarp();
@@ -213,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * BN;
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
+      for (int sb = 0; sb < p.stage_blocks; ++sb) {
         bool f = (lane == 0) ? mbar_wait(&full_bar[stage], phase, p.timeout, abort_flag) : true;
         f = __shfl_sync(0xffffffffu, f, 0);
         if (!f) {
@@ -223,24 +244,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t a_base = smem_u32(sA + stage * Cfg::kABytes);
-          const uint32_t b_base = smem_u32(sB + stage * Cfg::kBBytes);
+          const uint32_t a_base = smem_u32(sA + stage * A_ST);
+          const uint32_t b_base = smem_u32(sB + stage * B_ST);
+          for (int j = 0; j < p.kbs; ++j) {
 #pragma unroll
-          for (int k = 0; k < kKBytes / kUmmaKBytes; ++k) {
-            const uint64_t adesc = sdesc_kmajor_sw128(a_base + k * kUmmaKBytes);
-            uint64_t bdesc;
-            if constexpr (B_MN) {
-              // UMMA K step = kUmmaK rows of K = kUmmaK/8 swizzle atoms of 1024 B.
-              bdesc = sdesc_mnmajor_sw128(b_base + k * (Cfg::kUmmaK / 8) * 1024,
-                                          Cfg::kBKElems * 128);
-            } else {
-              bdesc = sdesc_kmajor_sw128(b_base + k * kUmmaKBytes);
+            for (int k = 0; k < kKBytes / kUmmaKBytes; ++k) {
+              const uint64_t adesc = sdesc_kmajor_sw128(a_base + j * Cfg::kABytes + k * kUmmaKBytes);
+              const uint32_t accum = (sb > 0 || j > 0 || k > 0) ? 1u : 0u;
+              if constexpr (B_MN) {
+                // UMMA K step = kUmmaK rows of K = kUmmaK/8 swizzle atoms of 1024 B.
+                const uint64_t bdesc = sdesc_mnmajor_sw128(b_base + k * (Cfg::kUmmaK / 8) * 1024,
+                                                           Cfg::kBKElems * 128);
+                if constexpr (KIND == 2)
+                  umma_i8(d_tmem, adesc, bdesc, Cfg::kIdesc, accum);
+                else
+                  umma_f16(d_tmem, adesc, bdesc, Cfg::kIdesc, accum);
+              } else if constexpr (SWIGLU) {
+                // gate rows and up rows are separate boxes: two N/2 products
+                const uint32_t hb = (BN / 2) * kKBytes;
+                const uint64_t gdesc = sdesc_kmajor_sw128(b_base + j * hb + k * kUmmaKBytes);
+                const uint64_t udesc =
+                    sdesc_kmajor_sw128(b_base + B_ST / 2 + j * hb + k * kUmmaKBytes);
+                umma_f16(d_tmem, adesc, gdesc, Cfg::kIdescHalf, accum);
+                umma_f16(d_tmem + BN / 2, adesc, udesc, Cfg::kIdescHalf, accum);
+              } else {
+                const uint64_t bdesc =
+                    sdesc_kmajor_sw128(b_base + j * Cfg::kBBytes + k * kUmmaKBytes);
+                if constexpr (KIND == 2)
+                  umma_i8(d_tmem, adesc, bdesc, Cfg::kIdesc, accum);
+                else
+                  umma_f16(d_tmem, adesc, bdesc, Cfg::kIdesc, accum);
+              }
             }
-            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
-            if constexpr (KIND == 2)
-              umma_i8(d_tmem, adesc, bdesc, Cfg::kIdesc, accum);
-            else
-              umma_f16(d_tmem, adesc, bdesc, Cfg::kIdesc, accum);
           }
           umma_commit(&empty_bar[stage]);  // frees the smem stage when read
           any_mma = true;

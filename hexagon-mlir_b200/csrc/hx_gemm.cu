@@ -121,6 +121,38 @@ int make_tmap(CUtensorMap *map, const void *ptr, int dtype, uint64_t inner, uint
   return HX_OK;
 }
 
+// 3-D view of a row-major matrix for multi-block K loads: x = `inner`
+// elements of one 128-byte K block, y = row, z = K block (stride 128 bytes).
+// Requires K to be a whole number of blocks (no tail inside a block).
+int make_tmap3(CUtensorMap *map, const void *ptr, int dtype, uint64_t inner, uint64_t rows,
+               uint64_t kblocks, uint64_t row_stride_elems, uint32_t box_rows, uint32_t box_kb) {
+  auto enc = get_encode();
+  if (!enc) {
+    g_last_error = "cuTensorMapEncodeTiled unavailable";
+    return HX_E_CUDA;
+  }
+  CUtensorMapDataType dt;
+  uint64_t esz;
+  switch (dtype) {
+    case HX_F16: dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16; esz = 2; break;
+    case HX_BF16: dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; esz = 2; break;
+    case HX_S8: dt = CU_TENSOR_MAP_DATA_TYPE_UINT8; esz = 1; break;
+    default: return unsupported("tensor map dtype");
+  }
+  cuuint64_t dims[3] = {inner, rows, kblocks};
+  cuuint64_t strides[2] = {row_stride_elems * esz, inner * esz};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(inner), box_rows, box_kb};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, dt, 3, const_cast<void *>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    g_last_error = "cuTensorMapEncodeTiled (3-D) failed (code " + std::to_string(int(r)) + ")";
+    return HX_E_UNSUPPORTED;
+  }
+  return HX_OK;
+}
+
 int esize(int dtype) {
   switch (dtype) {
     case HX_F16:
@@ -161,7 +193,7 @@ int launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
               cudaStream_t s) {
   using Cfg = GemmCfg<BN, KIND, BMN, SW>;
   auto kern = hx_gemm_sm100_kernel<BN, KIND, BMN, SW>;
-  const int smem = Cfg::smem_bytes(p.stages);
+  const int smem = p.stages * p.kbs * Cfg::kStageBytes + 1024 + 256;
   static std::atomic<int> configured{0};
   if (configured.load(std::memory_order_acquire) < smem) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -353,8 +385,16 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
   if (bn == 0) bn = choose_bn(d->M, d->N, swiglu, bmn && ez == 1, sms);
   if (bn != 64 && bn != 128 && bn != 256) return arg_fail("tile_n must be 64, 128 or 256");
   if (bmn && ez == 1 && bn < 128) return unsupported("tile_n 64 with int8 B[K,N]");
+  // Several 128-byte K blocks per TMA instruction when K is whole blocks:
+  // the per-instruction cost of TMA, not bytes, limits small boxes.
+  const bool use3d = !bmn && (d->K * ez) % kKBytes == 0;
+  // Narrow tiles gain most (their boxes are smallest); wide tiles keep depth.
+  int kbs = !use3d ? 1 : (bn == 64 ? 4 : (bn == 128 ? 2 : 1));
   int stages = d->stages;
-  const int max_stages = std::min(8, (kMaxDynSmem - 1280) / stage_bytes(bn));
+  auto fit = [&](int kb) { return std::min(8, (kMaxDynSmem - 1280) / (kb * stage_bytes(bn))); };
+  // an explicit stage count takes precedence: fewer K blocks per load until it fits
+  while (kbs > 1 && fit(kbs) < std::max(2, stages)) kbs >>= 1;
+  const int max_stages = fit(kbs);
   if (stages == 0) stages = max_stages;
   if (stages < 2 || stages > max_stages) return arg_fail("stages out of range for tile_n");
 
@@ -363,6 +403,14 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
   const int out_w = swiglu ? bn / 2 : bn;
 
   CUtensorMap ta, tb;
+  if (use3d) {
+    const uint64_t kblocks = static_cast<uint64_t>(d->K) / bk;
+    rc = make_tmap3(&ta, d->A, d->a_dtype, bk, d->M, kblocks, d->lda, kBM, kbs);
+    if (rc != HX_OK) return rc;
+    const uint64_t rows = swiglu ? 2 * d->N : d->N;
+    rc = make_tmap3(&tb, d->B, d->b_dtype, bk, rows, kblocks, d->ldb, swiglu ? bn / 2 : bn, kbs);
+    if (rc != HX_OK) return rc;
+  } else {
   rc = make_tmap(&ta, d->A, d->a_dtype, d->K, d->M, d->lda, bk, kBM);
   if (rc != HX_OK) return rc;
   if (bmn) {
@@ -372,6 +420,7 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
     rc = make_tmap(&tb, d->B, d->b_dtype, d->K, rows, d->ldb, bk, swiglu ? bn / 2 : bn);
   }
   if (rc != HX_OK) return rc;
+  }
 
   GemmParams p;
   p.M = static_cast<int32_t>(d->M);
@@ -385,6 +434,9 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
   if (total > INT32_MAX) return unsupported("too many tiles");
   p.total_tiles = static_cast<int32_t>(total);
   p.stages = stages;
+  p.kbs = kbs;
+  p.stage_blocks = (p.k_blocks + kbs - 1) / kbs;
+  p.use3d = use3d ? 1 : 0;
   p.timeout = d->timeout_cycles ? d->timeout_cycles : kDefaultTimeout;
   p.err_flag = d->error_flag;
   p.epi = make_epi(d);

@@ -72,7 +72,18 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
-// Same, with an L2 eviction-priority hint (createpolicy result).
+// 3-D tiled bulk tensor load (x innermost).  Used with a map whose third
+// dimension steps 128 bytes along K, so one instruction fetches several
+// consecutive 128-byte K blocks of a tile, stored block after block.
+__device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *map, uint64_t *bar,
+                                            int32_t x, int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+// Same as tma_load_2d, with an L2 eviction-priority hint (createpolicy result).
 __device__ __forceinline__ void tma_load_2d_hint(void *smem_dst, const CUtensorMap *map,
                                                  uint64_t *bar, int32_t x, int32_t y,
                                                  uint64_t policy) {
