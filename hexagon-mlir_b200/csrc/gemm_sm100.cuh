@@ -49,6 +49,7 @@ struct GemmParams {
   int32_t kbs;                    // 128-byte K blocks per stage (one TMA load each for A, B)
   int32_t stage_blocks;           // stages per tile: ceil(k_blocks / kbs)
   int32_t use3d;                  // 3-D maps (K blocks as the third dimension)
+  int32_t splits;                 // split-K: CTAs per cluster sharing one tile (1 = none)
   uint64_t timeout;               // cycles per bounded wait
   int32_t *err_flag;              // optional global error word
   EpiArgs epi;
@@ -68,6 +69,7 @@ struct GemmCfg {
   static constexpr int smem_bytes(int stages) { return stages * kStageBytes + 1024 /*align*/ + 256 /*bars*/; }
   static constexpr uint32_t kIdesc = make_idesc(KIND, B_MN, kBM, BN);
   static constexpr uint32_t kIdescHalf = make_idesc(KIND, B_MN, kBM, BN / 2);  // SWIGLU halves
+  static constexpr int kPartBytes = kBM * (BN + 4) * 4;  // split-K partial tile
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
   static_assert(!(SWIGLU && B_MN), "SWIGLU needs the W[N,K] layout");
   static_assert(kTmemCols >= 32 && kTmemCols <= 512, "TMEM columns");
@@ -81,6 +83,34 @@ __device__ __forceinline__ void tile_coords(int t, const GemmParams &p, int &m_b
   const int r = t - g * per_group;
   m_blk = first_m + r % gsize;
   n_blk = r / gsize;
+}
+
+__device__ __forceinline__ uint32_t gemm_cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void gemm_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ uint32_t gemm_peer_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void ld_cluster_v4(uint32_t addr, uint32_t &a, uint32_t &b, uint32_t &c,
+                                              uint32_t &d) {
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+               : "r"(addr)
+               : "memory");
 }
 
 __device__ __forceinline__ void raise_abort(volatile int *abort_flag, int32_t *err, int code) {
@@ -103,7 +133,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int B_ST = p.kbs * Cfg::kBBytes;  // bytes of B per stage
   uint8_t *sA = smem;
   uint8_t *sB = smem + STAGES * A_ST;
-  uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + STAGES * (A_ST + B_ST));
+  // Split-K parks a [128][BN + 4] fp32 partial over the ring: the barriers
+  // go after whichever of the two is larger.
+  const int ring_bytes = STAGES * (A_ST + B_ST);
+  const int part_bytes = p.splits > 1 ? Cfg::kPartBytes : 0;
+  uint64_t *full_bar =
+      reinterpret_cast<uint64_t *>(smem + (ring_bytes > part_bytes ? ring_bytes : part_bytes));
   uint64_t *empty_bar = full_bar + STAGES;
   uint64_t *tfull_bar = empty_bar + STAGES;   // [2]
   uint64_t *tempty_bar = tfull_bar + 2;       // [2]
@@ -144,17 +179,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   grid_dep_launch_dependents();
   grid_dep_wait();
 
+  // Split-K: the CTAs of a cluster share each tile; CTA `rank` streams stage
+  // blocks [sb_begin, sb_end) of it.  Without split-K: the whole K range.
+  const int S = p.splits;
+  const uint32_t rank = S > 1 ? gemm_cluster_rank() : 0u;
+  const int t_first = blockIdx.x / S, t_step = gridDim.x / S;
+  const int sper = p.stage_blocks / S, srem = p.stage_blocks % S;
+  const int sb_begin = static_cast<int>(rank) * sper + min(static_cast<int>(rank), srem);
+  const int sb_end = sb_begin + sper + (static_cast<int>(rank) < srem ? 1 : 0);
+
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     int stage = 0;
     uint32_t phase = 0;
     int64_t issued = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+    for (int t = t_first; t < p.total_tiles && ok; t += t_step) {
       int m_blk, n_blk;
       tile_coords(t, p, m_blk, n_blk);
       const int m0 = m_blk * kBM;
-      for (int sb = 0; sb < p.stage_blocks; ++sb) {
+      for (int sb = sb_begin; sb < sb_end; ++sb) {
         bool w = (lane == 0) ? mbar_wait(&empty_bar[stage], phase ^ 1, p.timeout, abort_flag)
                              : true;
         w = __shfl_sync(0xffffffffu, w, 0);
@@ -221,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int it = 0;
     bool ok = true;
     bool any_mma = false;
-    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x, ++it) {
+    for (int t = t_first; t < p.total_tiles && ok; t += t_step, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       bool w = (lane == 0) ? mbar_wait(&tempty_bar[acc], acc_phase ^ 1, p.timeout, abort_flag)
@@ -234,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * BN;
-      for (int sb = 0; sb < p.stage_blocks; ++sb) {
+      for (int sb = sb_begin; sb < sb_end; ++sb) {
         bool f = (lane == 0) ? mbar_wait(&full_bar[stage], phase, p.timeout, abort_flag) : true;
         f = __shfl_sync(0xffffffffu, f, 0);
         if (!f) {
@@ -250,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int k = 0; k < kKBytes / kUmmaKBytes; ++k) {
               const uint64_t adesc = sdesc_kmajor_sw128(a_base + j * Cfg::kABytes + k * kUmmaKBytes);
-              const uint32_t accum = (sb > 0 || j > 0 || k > 0) ? 1u : 0u;
+              const uint32_t accum = (sb > sb_begin || j > 0 || k > 0) ? 1u : 0u;
               if constexpr (B_MN) {
                 // UMMA K step = kUmmaK rows of K = kUmmaK/8 swizzle atoms of 1024 B.
                 const uint64_t bdesc = sdesc_mnmajor_sw128(b_base + k * (Cfg::kUmmaK / 8) * 1024,
@@ -301,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;                   // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
     int it = 0;
-    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+    for (int t = t_first; t < p.total_tiles; t += t_step, ++it) {
       int m_blk, n_blk;
       tile_coords(t, p, m_blk, n_blk);
       const int acc = it & 1;
@@ -315,6 +359,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int m = m_blk * kBM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      if (S > 1) {
+        // Split-K: park this CTA's partial accumulator (all BN columns, raw
+        // fp32 / int32 bits) in its own smem, row-major [128][BN + 4] (the pad
+        // spreads rows over banks); the stage ring is idle once the tile's
+        // last UMMA has completed.
+        uint32_t *part = reinterpret_cast<uint32_t *>(smem) + row_in_tile * (BN + 4);
+#pragma unroll 1
+        for (int c = (warp - 2) / 4; c < BN / 32; c += 2) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<uint4 *>(part + c * 32 + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        continue;
+      }
 #pragma unroll 1
       for (int c = (warp - 2) / 4; c < Cfg::kBNOut / 32; c += 2) {
         uint32_t r[32];
@@ -348,6 +412,65 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+
+  if (S > 1) {
+    // Every CTA's partial is in its smem; each reduces the output column
+    // chunks it owns (chunk oc belongs to rank oc % S) over the S partials
+    // through distributed shared memory, applies the epilogue once, stores.
+    gemm_cluster_sync();
+    if (warp >= 2) {
+      const int q = warp & 3;
+      const int row_in_tile = q * 32 + lane;
+      const uint32_t part_base = smem_u32(smem);
+      const bool raw_int = (KIND == 2) && (p.epi.c_dtype == HX_S32) && (p.epi.epi == HX_EPI_NONE);
+      int owned = 0;
+      for (int t = t_first; t < p.total_tiles; t += t_step) {  // one tile per cluster
+        int m_blk, n_blk;
+        tile_coords(t, p, m_blk, n_blk);
+        const int m = m_blk * kBM + row_in_tile;
+#pragma unroll 1
+        for (int oc = static_cast<int>(rank); oc < Cfg::kBNOut / 32; oc += S, ++owned) {
+          if ((owned & 1) != (warp - 2) / 4) continue;  // two warps per row quarter
+          uint32_t r[32];
+          float v[32], up[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            r[j] = 0u;
+            v[j] = 0.f;
+            up[j] = 0.f;
+          }
+          const uint32_t row_off = static_cast<uint32_t>(row_in_tile * (BN + 4) * 4);
+          for (int rr = 0; rr < S; ++rr) {
+            const uint32_t base = gemm_peer_addr(part_base + row_off, rr);
+            uint32_t x[32], u[32];
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)  // eight independent 16-byte DSMEM loads
+              ld_cluster_v4(base + (oc * 32 + j) * 4, x[j], x[j + 1], x[j + 2], x[j + 3]);
+            if constexpr (SWIGLU) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                ld_cluster_v4(base + (BN / 2 + oc * 32 + j) * 4, u[j], u[j + 1], u[j + 2], u[j + 3]);
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if constexpr (KIND == 2) r[j] += x[j];
+              else v[j] += __uint_as_float(x[j]);
+              if constexpr (SWIGLU) up[j] += __uint_as_float(u[j]);
+            }
+          }
+          if constexpr (KIND == 2) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = static_cast<float>(static_cast<int32_t>(r[j]));
+          }
+          const int n0 = n_blk * Cfg::kBNOut + oc * 32;
+          if (!raw_int) epi_transform32(p.epi, v, up, m, n0);
+          epi_store32(p.epi, v, r, raw_int, m, n0);
+        }
+      }
+    }
+    gemm_cluster_sync();  // peers keep their smem until every CTA has read it
+  }
+
   if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
 }
 

@@ -166,6 +166,7 @@ int esize(int dtype) {
 __host__ __device__ inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in limit per block on sm_100
+constexpr int kNeedsNoSplit = 1;     // internal: split-K clusters would not all be resident
 constexpr uint64_t kDefaultTimeout = 4000000000ull;  // ~2 s at 2 GHz
 
 // ------------------------------------------------------------ launch
@@ -193,7 +194,9 @@ int launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
               cudaStream_t s) {
   using Cfg = GemmCfg<BN, KIND, BMN, SW>;
   auto kern = hx_gemm_sm100_kernel<BN, KIND, BMN, SW>;
-  const int smem = p.stages * p.kbs * Cfg::kStageBytes + 1024 + 256;
+  const int ring = p.stages * p.kbs * Cfg::kStageBytes;
+  const int smem = std::max(ring, p.splits > 1 ? Cfg::kPartBytes : 0) + 1024 + 256;
+  if (smem > kMaxDynSmem) return unsupported("shared memory for this tile plan exceeds 227 KB");
   static std::atomic<int> configured{0};
   if (configured.load(std::memory_order_acquire) < smem) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -201,7 +204,36 @@ int launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     configured.store(kMaxDynSmem, std::memory_order_release);
   }
-  cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, ta, tb, p);
+  cudaError_t e;
+  if (p.splits > 1) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = p.splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // Split-K needs every cluster resident at once (one tile per cluster).
+    static std::atomic<int> max_clusters[9];
+    int mc = max_clusters[p.splits].load(std::memory_order_acquire);
+    if (mc == 0) {
+      e = cudaOccupancyMaxActiveClusters(&mc, kern, &cfg);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+      max_clusters[p.splits].store(std::max(mc, 1), std::memory_order_release);
+    }
+    if (grid / p.splits > mc) return kNeedsNoSplit;
+    cfg.numAttrs = 2;
+    e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  } else {
+    e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, ta, tb, p);
+  }
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "hx_gemm_sm100_kernel launch");
   return HX_OK;
@@ -233,24 +265,43 @@ int dispatch_kind(int bn, bool bmn, bool sw, const CUtensorMap &ta, const CUtens
 
 int stage_bytes(int bn) { return kBM * kKBytes + bn * kKBytes; }
 
-// Tile width choice: fewest waves x per-tile cost over the SMs, largest BN
-// on ties (a wider tile reuses each A tile over more columns).
-int choose_bn(int64_t M, int64_t n_out, bool swiglu, bool int8_kn, int sms) {
+// Tile plan: width BN (and, only when the caller asks, a split-K factor S).
+// Cost model calibrated on B200 measurements of the benchmark shapes: a
+// launch costs ~7 us of fixed latency (prologue, first loads, epilogue,
+// drain), after which each CTA streams its tiles' K blocks at ~100 GB/s of
+// TMA ingest (or the tensor rate, if slower); persistent CTAs overlap the
+// fixed part across waves.  Split-K adds ~3.5 us of DSMEM reduction.
+inline bool best_cost_found(double c) { return c < 1e299; }
+
+void plan_tiles(int64_t M, int64_t N, int64_t K, int ez, bool swiglu, bool bmn, int sms, int &bn,
+                int &splits, int split_req) {
   const int64_t m_tiles = (M + kBM - 1) / kBM;
-  int best = 256;
-  int64_t best_cost = INT64_MAX;
-  for (int bn : {256, 128, 64}) {
-    if (int8_kn && bn < 128) continue;
-    const int out_w = swiglu ? bn / 2 : bn;
-    const int64_t tiles = m_tiles * ((n_out + out_w - 1) / out_w);
-    const int64_t waves = (tiles + sms - 1) / sms;
-    const int64_t cost = waves * (out_w + 64);
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = bn;
+  const int64_t k_blocks = (K * ez + kKBytes - 1) / kKBytes;
+  const double flop_per_us_sm = 10.9e6 * (ez == 1 ? 2.0 : 1.0);
+  double best = 1e300;
+  int best_bn = bn ? bn : 128, best_s = 1;
+  for (int b : {256, 128, 64}) {
+    if (bn && b != bn) continue;
+    if (bmn && ez == 1 && b < 128) continue;
+    const int out_w = swiglu ? b / 2 : b;
+    const int64_t tiles = m_tiles * ((N + out_w - 1) / out_w);
+    for (int sp : {1, 2, 3, 4, 6, 8}) {
+      if (split_req == 0 ? sp != 1 : sp != split_req) continue;  // auto: no split
+      if (sp > 1 && (bmn || tiles * sp > sms || sp > k_blocks)) continue;
+      const int64_t waves = (tiles * sp + sms - 1) / sms;
+      const double kb = static_cast<double>((k_blocks + sp - 1) / sp);
+      const double ingest = kb * stage_bytes(b) / 100e3;
+      const double mma = kb * (2.0 * kBM * b * (kKBytes / ez)) / flop_per_us_sm;
+      const double cost = 7.0 + waves * std::max(ingest, mma) + (sp > 1 ? 3.5 : 0.0);
+      if (cost < best * 0.97) {  // prefer the earlier (wider) option on near ties
+        best = cost;
+        best_bn = b;
+        best_s = sp;
+      }
     }
   }
-  return best;
+  bn = best_bn;
+  splits = best_cost_found(best) ? best_s : (split_req > 1 ? split_req : 1);
 }
 
 int validate(const hx_gemm_desc *d) {
@@ -381,8 +432,13 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
                       (d->lda * ez) % 16 == 0 && (d->ldb * ez) % 16 == 0;
   if (!tma_ok) return run_simt(d, s);
 
+  if (d->split_k < 0 || d->split_k > 8) return arg_fail("split_k must be 0..8");
   int bn = d->tile_n;
-  if (bn == 0) bn = choose_bn(d->M, d->N, swiglu, bmn && ez == 1, sms);
+  int splits = d->split_k > 0 ? d->split_k : 1;
+  if (bmn) splits = 1;  // split-K is built for the W[N,K] path
+  if (bn == 0 || d->split_k == 0) {
+    plan_tiles(d->M, d->N, d->K, ez, swiglu, bmn, sms, bn, splits, d->split_k);
+  }
   if (bn != 64 && bn != 128 && bn != 256) return arg_fail("tile_n must be 64, 128 or 256");
   if (bmn && ez == 1 && bn < 128) return unsupported("tile_n 64 with int8 B[K,N]");
   // Several 128-byte K blocks per TMA instruction when K is whole blocks:
@@ -437,19 +493,34 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
   p.kbs = kbs;
   p.stage_blocks = (p.k_blocks + kbs - 1) / kbs;
   p.use3d = use3d ? 1 : 0;
+  p.splits = splits;
   p.timeout = d->timeout_cycles ? d->timeout_cycles : kDefaultTimeout;
   p.err_flag = d->error_flag;
   p.epi = make_epi(d);
 
+  if (splits > 1 && (total * splits > sms || splits > p.stage_blocks)) {
+    if (d->split_k > 1) return unsupported("split_k: tiles x split_k exceeds the SMs or the K blocks");
+    splits = p.splits = 1;
+  }
   int ctas = sms;
   if (d->max_ctas > 0) ctas = std::min(ctas, static_cast<int>(d->max_ctas));
-  const int grid = static_cast<int>(std::min<int64_t>(total, ctas));
-
-  switch (kind) {
-    case 0: return dispatch_kind<0>(bn, bmn, swiglu, ta, tb, p, grid, s);
-    case 1: return dispatch_kind<1>(bn, bmn, swiglu, ta, tb, p, grid, s);
-    default: return dispatch_kind<2>(bn, bmn, swiglu, ta, tb, p, grid, s);
+  int grid = splits > 1 ? static_cast<int>(total * splits)
+                        : static_cast<int>(std::min<int64_t>(total, ctas));
+  auto dispatch = [&]() {
+    switch (kind) {
+      case 0: return dispatch_kind<0>(bn, bmn, swiglu, ta, tb, p, grid, s);
+      case 1: return dispatch_kind<1>(bn, bmn, swiglu, ta, tb, p, grid, s);
+      default: return dispatch_kind<2>(bn, bmn, swiglu, ta, tb, p, grid, s);
+    }
+  };
+  int r = dispatch();
+  if (r == kNeedsNoSplit) {  // clusters would not all fit at once: run unsplit
+    if (d->split_k > 1) return unsupported("split_k clusters do not all fit on the GPU at once");
+    p.splits = 1;
+    grid = static_cast<int>(std::min<int64_t>(total, ctas));
+    r = dispatch();
   }
+  return r;
 }
 
 // ------------------------------------------------------------ W8A16

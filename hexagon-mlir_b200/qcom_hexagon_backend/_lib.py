@@ -87,6 +87,8 @@ class HxGemmDesc(ctypes.Structure):
         ("force_simt", ctypes.c_int32),
         ("error_flag", ctypes.c_void_p),
         ("timeout_cycles", ctypes.c_uint64),
+        ("split_k", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
     ]
 
 

@@ -77,6 +77,7 @@ def gemm(
     force_simt: bool = False,
     error_flag: Optional[torch.Tensor] = None,
     timeout_cycles: int = 0,
+    split_k: int = 0,
 ) -> torch.Tensor:
     """out = epilogue(a @ B) with B = b.T (b_layout "nk", b is W[N,K]) or
     B = b (b_layout "kn", b is [K,N]).
@@ -87,7 +88,7 @@ def gemm(
     d, out, dev = make_desc(a, b, b_layout=b_layout, out=out, out_dtype=out_dtype, epilogue=epilogue,
                             bias=bias, residual=residual, scale=scale, tile_n=tile_n, stages=stages,
                             max_ctas=max_ctas, force_simt=force_simt, error_flag=error_flag,
-                            timeout_cycles=timeout_cycles)
+                            timeout_cycles=timeout_cycles, split_k=split_k)
     rec = _recorder
     if rec is not None and rec.device == dev:
         if rec.accepts(d, a, b, residual, b_layout, tile_n, stages, max_ctas, force_simt):
@@ -211,7 +212,7 @@ def chain_flush(*args):
 
 def make_desc(a, b, *, b_layout="nk", out=None, out_dtype=None, epilogue="none", bias=None,
               residual=None, scale=None, tile_n=0, stages=0, max_ctas=0, force_simt=False,
-              error_flag=None, timeout_cycles=0):
+              error_flag=None, timeout_cycles=0, split_k=0):
     """Validate the tensors and fill an hx_gemm_desc; returns (desc, out, device).
     The tensors must stay alive while the descriptor is in use."""
     _check_cuda(a, "a")
@@ -281,6 +282,7 @@ def make_desc(a, b, *, b_layout="nk", out=None, out_dtype=None, epilogue="none",
             raise ValueError("error_flag must be an int32 CUDA tensor")
         d.error_flag = error_flag.data_ptr()
     d.timeout_cycles = timeout_cycles
+    d.split_k = split_k
     return d, out, dev
 
 

@@ -104,6 +104,10 @@ typedef struct hx_gemm_desc {
   int32_t *error_flag;     /* optional device int32; set non-zero by a kernel
                               whose bounded wait ran out                      */
   uint64_t timeout_cycles; /* bound for each device wait (0 = ~2 s default)   */
+  int32_t split_k;         /* CTAs (2..8, one thread-block cluster) sharing a
+                              tile's K range, partials reduced through
+                              distributed shared memory; 1 = off, 0 = auto   */
+  int32_t reserved0;
 } hx_gemm_desc;
 
 /* C = epilogue(A . B).  Replaces the linalg.matmul + linalg.generic pair the

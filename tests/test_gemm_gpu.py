@@ -364,3 +364,36 @@ def test_w8a16_grouped_chain(cuda_device, M):
         xr = refs[dep].astype(np.float16) if dep >= 0 else to_np32(xin)
         refs.append(O.w8a16_ref(xr, w.numpy(), s.numpy()))
         assert_close(to_np32(ys[i]), refs[-1])
+
+
+# ---------------------------------------------------------------- split-K (cluster DSMEM reduction)
+@pytest.mark.parametrize("split_k", [2, 3, 4, 8])
+@pytest.mark.parametrize("epilogue", ["none", "bias_residual", "bias_gelu_tanh", "swiglu"])
+def test_split_k_epilogues(cuda_device, split_k, epilogue):
+    run_and_check(256, 384, 2048, torch.float16, epilogue, split_k=split_k, tile_n=128, seed=40 + split_k)
+
+
+@pytest.mark.parametrize("shape", [(512, 384, 3072), (200, 300, 1000), (130, 520, 4096)],
+                         ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("tile_n", [64, 128, 256])
+def test_split_k_shapes(cuda_device, shape, tile_n):
+    """K tails (2-D maps, one block per load), M/N tails, every tile width."""
+    M, N, K = shape
+    run_and_check(M, N, K, torch.bfloat16, "bias", split_k=3, tile_n=tile_n, seed=41)
+
+
+def test_split_k_int8_exact(cuda_device):
+    q = hx()
+    g = torch.Generator().manual_seed(42)
+    a = torch.randint(-127, 128, (256, 4096), generator=g, dtype=torch.int64).to(torch.int8)
+    w = torch.randint(-127, 128, (512, 4096), generator=g, dtype=torch.int64).to(torch.int8)
+    out = q.gemm(a.cuda(), w.cuda(), split_k=4, tile_n=256)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), O.int8_gemm_exact(a.numpy(), w.numpy()))
+
+
+def test_split_k_rejects_oversubscription(cuda_device):
+    q = hx()
+    a, w, _, _ = make_inputs(4096, 4096, 256, torch.float16)
+    with pytest.raises(q._lib.HexagonB200Error):
+        q.gemm(a, w, split_k=8)  # 1024 tiles x 8 CTAs cannot be resident
