@@ -22,6 +22,7 @@
 #include "gemm_chain.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_sm100.cuh"
+#include "gemm_sm100_2sm.cuh"
 #include "gemv_grouped.cuh"
 #include "gemv_w8a16.cuh"
 #include "w8a16_sm100.cuh"
@@ -239,6 +240,48 @@ int launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
   return HX_OK;
 }
 
+template <int BN, int KIND, bool SW>
+int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p, int grid,
+                cudaStream_t s) {
+  auto kern = hx_gemm_sm100_2sm_kernel<BN, KIND, SW>;
+  const int stage = p.kbs * (kBM * kKBytes + (BN / 2) * kKBytes);
+  const int smem = p.stages * stage + 1024 + 256;
+  if (smem > kMaxDynSmem) return unsupported("shared memory for this pair plan exceeds 227 KB");
+  static std::atomic<int> configured{0};
+  if (!configured.load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pair)");
+    configured.store(1, std::memory_order_release);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "hx_gemm_sm100_2sm_kernel launch");
+  return HX_OK;
+}
+
+int dispatch_pair(int kind, int bn, bool sw, const CUtensorMap &ta, const CUtensorMap &tb,
+                  const GemmParams &p, int grid, cudaStream_t s) {
+  if (bn != 256) return unsupported("pair tiles use tile_n 256");
+  if (kind == 0) return sw ? launch_pair<256, 0, true>(ta, tb, p, grid, s) : launch_pair<256, 0, false>(ta, tb, p, grid, s);
+  if (kind == 1) return sw ? launch_pair<256, 1, true>(ta, tb, p, grid, s) : launch_pair<256, 1, false>(ta, tb, p, grid, s);
+  if (sw) return unsupported("SWIGLU with int8 inputs");
+  return launch_pair<256, 2, false>(ta, tb, p, grid, s);
+}
+
 template <int KIND, bool BMN, bool SW>
 int dispatch_bn(int bn, const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
                 int grid, cudaStream_t s) {
@@ -444,10 +487,22 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
   // Several 128-byte K blocks per TMA instruction when K is whole blocks:
   // the per-instruction cost of TMA, not bytes, limits small boxes.
   const bool use3d = !bmn && (d->K * ez) % kKBytes == 0;
+  // CTA pairs (256 x 256 tiles, cta_group::2) for GEMMs with at least a wave
+  // of pair tiles: each SM then ingests 1/3 fewer bytes per flop.
+  bool pair = false;
+  {
+    const int64_t pair_tiles = ((d->M + 2 * kBM - 1) / (2 * kBM)) * ((d->N + (swiglu ? 127 : 255)) / (swiglu ? 128 : 256));
+    pair = use3d && splits == 1 && d->tile_n == 0 && d->stages == 0 && d->max_ctas == 0 &&
+           pair_tiles >= sms / 2;
+    if (const char *env = std::getenv("HX_GEMM_PAIR")) pair = pair || (use3d && std::atoi(env) > 0 && splits == 1);
+    if (const char *env = std::getenv("HX_GEMM_PAIR")) if (std::atoi(env) == 0) pair = false;
+    if (pair) bn = 256;
+  }
   // Narrow tiles gain most (their boxes are smallest); wide tiles keep depth.
-  int kbs = !use3d ? 1 : (bn == 64 ? 4 : (bn == 128 ? 2 : 1));
+  int kbs = !use3d ? 1 : (bn == 64 ? 4 : (bn == 128 ? 2 : (pair ? 2 : 1)));
   int stages = d->stages;
-  auto fit = [&](int kb) { return std::min(8, (kMaxDynSmem - 1280) / (kb * stage_bytes(bn))); };
+  const int per_stage = pair ? kBM * kKBytes + (bn / 2) * kKBytes : stage_bytes(bn);
+  auto fit = [&](int kb) { return std::min(8, (kMaxDynSmem - 1280) / (kb * per_stage)); };
   // an explicit stage count takes precedence: fewer K blocks per load until it fits
   while (kbs > 1 && fit(kbs) < std::max(2, stages)) kbs >>= 1;
   const int max_stages = fit(kbs);
@@ -464,7 +519,7 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
     rc = make_tmap3(&ta, d->A, d->a_dtype, bk, d->M, kblocks, d->lda, kBM, kbs);
     if (rc != HX_OK) return rc;
     const uint64_t rows = swiglu ? 2 * d->N : d->N;
-    rc = make_tmap3(&tb, d->B, d->b_dtype, bk, rows, kblocks, d->ldb, swiglu ? bn / 2 : bn, kbs);
+    rc = make_tmap3(&tb, d->B, d->b_dtype, bk, rows, kblocks, d->ldb, (swiglu || pair) ? bn / 2 : bn, kbs);
     if (rc != HX_OK) return rc;
   } else {
   rc = make_tmap(&ta, d->A, d->a_dtype, d->K, d->M, d->lda, bk, kBM);
@@ -481,7 +536,7 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
   GemmParams p;
   p.M = static_cast<int32_t>(d->M);
   p.K = static_cast<int32_t>(d->K);
-  p.m_tiles = static_cast<int32_t>((d->M + kBM - 1) / kBM);
+  p.m_tiles = static_cast<int32_t>((d->M + (pair ? 2 * kBM : kBM) - 1) / (pair ? 2 * kBM : kBM));
   p.n_tiles = static_cast<int32_t>((d->N + out_w - 1) / out_w);
   p.k_blocks = static_cast<int32_t>((d->K + bk - 1) / bk);
   p.n_half = static_cast<int32_t>(d->N);
@@ -513,6 +568,10 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
       default: return dispatch_kind<2>(bn, bmn, swiglu, ta, tb, p, grid, s);
     }
   };
+  if (pair) {
+    const int pairs = static_cast<int>(std::min<int64_t>(total, sms / 2));
+    return dispatch_pair(kind, bn, swiglu, ta, tb, p, 2 * pairs, s);
+  }
   int r = dispatch();
   if (r == kNeedsNoSplit) {  // clusters would not all fit at once: run unsplit
     if (d->split_k > 1) return unsupported("split_k clusters do not all fit on the GPU at once");

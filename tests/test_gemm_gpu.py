@@ -397,3 +397,38 @@ def test_split_k_rejects_oversubscription(cuda_device):
     a, w, _, _ = make_inputs(4096, 4096, 256, torch.float16)
     with pytest.raises(q._lib.HexagonB200Error):
         q.gemm(a, w, split_k=8)  # 1024 tiles x 8 CTAs cannot be resident
+
+
+# ---------------------------------------------------------------- CTA pairs (cta_group::2)
+@pytest.fixture
+def force_pairs():
+    os.environ["HX_GEMM_PAIR"] = "1"
+    yield
+    del os.environ["HX_GEMM_PAIR"]
+
+
+@pytest.mark.parametrize("epilogue", ["none", "bias", "bias_gelu_tanh", "bias_residual", "swiglu"])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+def test_pair_tiles(cuda_device, force_pairs, epilogue, dtype):
+    run_and_check(640, 768, 512, dtype, epilogue, seed=50)
+
+
+@pytest.mark.parametrize("shape", [(256, 256, 64), (300, 520, 192), (1024, 1000, 1024), (129, 2048, 128)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_pair_tile_shapes(cuda_device, force_pairs, shape):
+    run_and_check(*shape, torch.bfloat16, "bias", seed=51)
+
+
+def test_pair_int8_exact(cuda_device, force_pairs):
+    q = hx()
+    g = torch.Generator().manual_seed(52)
+    a = torch.randint(-127, 128, (600, 1024), generator=g, dtype=torch.int64).to(torch.int8)
+    w = torch.randint(-127, 128, (520, 1024), generator=g, dtype=torch.int64).to(torch.int8)
+    out = q.gemm(a.cuda(), w.cuda())
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), O.int8_gemm_exact(a.numpy(), w.numpy()))
+
+
+def test_pair_default_for_large_gemm(cuda_device):
+    """A GEMM with a full wave of 256x256 tiles takes the pair kernel by default."""
+    run_and_check(4096, 4096, 1024, torch.bfloat16, "none", seed=53)
