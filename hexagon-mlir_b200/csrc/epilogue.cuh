@@ -9,7 +9,10 @@
 //
 // Math follows the reference's golden (PyTorch): F.gelu(approximate="tanh")
 // (test/python/triton/test_gelu.py:72) and F.silu (test_silu.py:63), both
-// evaluated in fp32 (CUDA's __expf; GELU through an exact identity below).
+// evaluated in fp32.  For fp32 outputs through CUDA's __expf (GELU via an
+// exact identity below); for 16-bit outputs through the hardware tanh.approx
+// (relative error about 2^-11, below half an fp16 ulp of the result scale),
+// one special-function op per element instead of two.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -32,6 +35,9 @@ struct EpiArgs {
   int32_t r_vec_ok;    // residual rows are 16-byte aligned
   int32_t b_vec_ok;    // bias is 16-byte aligned
   int32_t s_vec_ok;    // scale is 16-byte aligned
+  int32_t pre16;       // every operand the epilogue reads (scale, bias,
+                       // residual) is 16-bit and 16-byte aligned: full
+                       // 32-column chunks may be prefetched raw (Pre16)
 };
 
 __device__ __forceinline__ float ld_as_float(const void *p, int dtype, int64_t i) {
@@ -54,6 +60,24 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return __fdividef(x, 1.f + __expf(-y));
 }
 __device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.f + __expf(-x)); }
+
+__device__ __forceinline__ float tanh_hw(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// 0.5 x (1 + tanh(y)) with one hardware tanh (16-bit outputs).
+__device__ __forceinline__ float gelu_tanh_hw(float x) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
+  const float k1 = 0.044715f;
+  const float hx = 0.5f * x;
+  return fmaf(hx, tanh_hw(k0 * fmaf(k1 * x, x * x, x)), hx);
+}
+// x * sigmoid(x) = 0.5 x (1 + tanh(x / 2)).
+__device__ __forceinline__ float silu_hw(float x) {
+  const float hx = 0.5f * x;
+  return fmaf(hx, tanh_hw(hx), hx);
+}
 
 // Load 32 consecutive elements v[j] = p[n0 + j] as float, j < 32 (columns
 // >= N read as 0).  `vec_ok`: p is 16-byte aligned (n0 is a multiple of 32).
@@ -99,6 +123,120 @@ __device__ __forceinline__ void load_row32(const void *p, int dtype, int64_t bas
   for (int j = 0; j < 32; ++j) v[j] = (n0 + j < N) ? ld_as_float(p, dtype, base + n0 + j) : 0.f;
 }
 
+// Final activation of BIAS_GELU_TANH / BIAS_SILU (identity otherwise).
+__device__ __forceinline__ void epi_activate32(const EpiArgs &e, float (&v)[32]) {
+  const bool hw = (e.c_dtype != HX_F32);
+  if (e.epi == HX_EPI_BIAS_GELU_TANH) {
+    if (hw) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_hw(v[j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+    }
+  } else if (e.epi == HX_EPI_BIAS_SILU) {
+    if (hw) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = silu_hw(v[j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = silu(v[j]);
+    }
+  }
+}
+
+__device__ __forceinline__ void swiglu32(const EpiArgs &e, float (&v)[32], const float (&up)[32]) {
+  if (e.c_dtype != HX_F32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = silu_hw(v[j]) * up[j];
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = silu(v[j]) * up[j];
+  }
+}
+
+// Raw 16-bit operands of one full 32-column chunk, loaded ahead of the
+// accumulator so their global-memory latency overlaps other work.
+//   a: scale (DEQUANT_SCALE) or bias;   b: bias (DEQUANT_SCALE) or residual row
+struct Pre16 {
+  uint4 a[4];
+  uint4 b[4];
+};
+
+template <bool COHERENT>
+__device__ __forceinline__ void ld_raw16x32(const void *p, int64_t off, uint4 (&w)[4]) {
+  const uint4 *q = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(p) + off);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = COHERENT ? __ldcg(q + i) : __ldg(q + i);
+}
+
+__device__ __forceinline__ void raw16_to_f32(const uint4 (&w)[4], int dtype, float (&t)[32]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t ws[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      if (dtype == HX_F16) {
+        const __half2 x = *reinterpret_cast<const __half2 *>(&ws[h]);
+        t[i * 8 + 2 * h] = __low2float(x);
+        t[i * 8 + 2 * h + 1] = __high2float(x);
+      } else {  // bf16: the value is the upper half of an fp32
+        t[i * 8 + 2 * h] = __uint_as_float(ws[h] << 16);
+        t[i * 8 + 2 * h + 1] = __uint_as_float(ws[h] & 0xffff0000u);
+      }
+    }
+  }
+}
+
+// Valid when e.pre16 and n0 + 32 <= e.N.
+__device__ __forceinline__ void epi_prefetch16(const EpiArgs &e, int m, int n0, Pre16 &f) {
+  const int epi = e.epi;
+  if (epi == HX_EPI_NONE || epi == HX_EPI_SWIGLU) return;
+  const bool residual = (epi == HX_EPI_BIAS_RESIDUAL || epi == HX_EPI_RESIDUAL);
+  if (epi == HX_EPI_DEQUANT_SCALE)
+    ld_raw16x32<false>(e.scale, n0, f.a);
+  else if (e.bias != nullptr && epi != HX_EPI_RESIDUAL)
+    ld_raw16x32<false>(e.bias, n0, f.a);
+  if (epi == HX_EPI_DEQUANT_SCALE && e.bias != nullptr)
+    ld_raw16x32<false>(e.bias, n0, f.b);
+  else if (residual && m < e.M)
+    ld_raw16x32<true>(e.residual, static_cast<int64_t>(m) * e.ldr + n0, f.b);
+}
+
+// epi_transform32 on prefetched operands.
+__device__ __forceinline__ void epi_apply16(const EpiArgs &e, float (&v)[32], const float (&up)[32],
+                                            int m, const Pre16 &f) {
+  const int epi = e.epi;
+  if (epi == HX_EPI_NONE) return;
+  if (epi == HX_EPI_SWIGLU) {
+    swiglu32(e, v, up);
+    return;
+  }
+  float t[32];
+  if (epi == HX_EPI_DEQUANT_SCALE) {
+    raw16_to_f32(f.a, e.scale_dtype, t);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] *= t[j];
+    if (e.bias != nullptr) {
+      raw16_to_f32(f.b, e.bias_dtype, t);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += t[j];
+    }
+    return;
+  }
+  if (e.bias != nullptr && epi != HX_EPI_RESIDUAL) {
+    raw16_to_f32(f.a, e.bias_dtype, t);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] += t[j];
+  }
+  if ((epi == HX_EPI_BIAS_RESIDUAL || epi == HX_EPI_RESIDUAL) && m < e.M) {
+    raw16_to_f32(f.b, e.c_dtype, t);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] += t[j];
+  }
+  epi_activate32(e, v);
+}
+
 // Apply the epilogue to 32 consecutive output columns of one row.
 //   v[j]   : accumulator for column n0 + j (gate half for SWIGLU)
 //   up[j]  : "up" accumulator for SWIGLU (ignored otherwise)
@@ -109,8 +247,7 @@ __device__ __forceinline__ void epi_transform32(const EpiArgs &e, float (&v)[32]
   const int epi = e.epi;
   if (epi == HX_EPI_NONE) return;
   if (epi == HX_EPI_SWIGLU) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = silu(v[j]) * up[j];
+    swiglu32(e, v, up);
     return;
   }
   float t[32];
@@ -129,13 +266,7 @@ __device__ __forceinline__ void epi_transform32(const EpiArgs &e, float (&v)[32]
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] += t[j];
   }
-  if (epi == HX_EPI_BIAS_GELU_TANH) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
-  } else if (epi == HX_EPI_BIAS_SILU) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = silu(v[j]);
-  }
+  epi_activate32(e, v);
 }
 
 // Store 32 float values (or raw int32 bits) of row m, columns n0.. n0+31.
@@ -226,6 +357,75 @@ __device__ __forceinline__ void epi_store_scalar(const EpiArgs &e, float v, int3
     case HX_S32: static_cast<int32_t *>(e.C)[i] = raw_int ? iv : __float2int_rn(v); break;
     default: break;
   }
+}
+
+
+// epi_store32 for a whole warp through its 4 KB staging buffer `stg`: each
+// thread parks its row segment in shared memory, then the warp writes 8 rows
+// x 64 B (16-bit C) or 4 rows x 128 B (32-bit C) per store instruction
+// instead of 32 rows x 16 B, a quarter of the L1 store wavefronts.  The 16-byte
+// chunks of a row are XOR-swizzled by row so both shared-memory phases are
+// free of bank conflicts.  All 32 lanes must call it with the same n0 and
+// m0 = the warp's first row; requires e.c_vec_ok and n0 + 32 <= e.N.
+__device__ __forceinline__ void epi_store32_staged(const EpiArgs &e, const float (&v)[32],
+                                                   const uint32_t (&raw)[32], bool raw_int, int m0,
+                                                   int n0, uint8_t *stg) {
+  const int lane = threadIdx.x & 31;
+  if (e.c_dtype == HX_F16 || e.c_dtype == HX_BF16) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (e.c_dtype == HX_F16) {
+        __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+        pk[j] = *reinterpret_cast<uint32_t *>(&h);
+      } else {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        pk[j] = *reinterpret_cast<uint32_t *>(&h);
+      }
+    }
+    uint8_t *row = stg + lane * 64;
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4 *>(row + ((q ^ sw) << 4)) =
+          make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+    __syncwarp();
+    const int qq = lane & 3;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = i * 8 + (lane >> 2);
+      const uint4 x = *reinterpret_cast<const uint4 *>(stg + r * 64 + ((qq ^ ((r >> 1) & 3)) << 4));
+      if (m0 + r < e.M)
+        *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(e.C) + static_cast<int64_t>(m0 + r) * e.ldc +
+                                   n0 + qq * 8) = x;
+    }
+  } else {
+    uint32_t w[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (e.c_dtype == HX_F32)
+        w[j] = __float_as_uint(v[j]);
+      else
+        w[j] = raw_int ? raw[j] : static_cast<uint32_t>(__float2int_rn(v[j]));
+    }
+    uint8_t *row = stg + lane * 128;
+    const int sw = lane & 7;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *reinterpret_cast<uint4 *>(row + ((q ^ sw) << 4)) =
+          make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+    __syncwarp();
+    const int qq = lane & 7;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = i * 4 + (lane >> 3);
+      const uint4 x = *reinterpret_cast<const uint4 *>(stg + r * 128 + ((qq ^ (r & 7)) << 4));
+      if (m0 + r < e.M)
+        *reinterpret_cast<uint4 *>(static_cast<uint32_t *>(e.C) + static_cast<int64_t>(m0 + r) * e.ldc +
+                                   n0 + qq * 4) = x;
+    }
+  }
+  __syncwarp();  // the next chunk may overwrite stg
 }
 
 }  // namespace hx

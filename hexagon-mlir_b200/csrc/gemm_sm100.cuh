@@ -38,6 +38,25 @@ constexpr int kKBytes = 128;      // K bytes per stage (one 128B swizzle row)
 constexpr int kUmmaKBytes = 32;   // K bytes per UMMA instruction
 constexpr int kThreads = 320;
 constexpr int kEpiWarps = 8;
+constexpr int kBarBytes = 256;                   // mbarriers + TMEM slot + abort word
+constexpr int kStageOutBytes = kEpiWarps * 4096; // per-epilogue-warp output staging
+
+// Per-phase %globaltimer stamps of each CTA (prologue, first stage, last UMMA,
+// accumulator ready, epilogue chunks) for latency studies; compiled in only
+// with -DHX_GEMM_TRACE.
+#ifdef HX_GEMM_TRACE
+__device__ unsigned long long g_gemm_trace[1024][16];
+#define HX_GEMM_STAMP(i)                                         \
+  do {                                                           \
+    unsigned long long t_;                                       \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));       \
+    if (blockIdx.x < 1024) g_gemm_trace[blockIdx.x][i] = t_;     \
+  } while (0)
+#else
+#define HX_GEMM_STAMP(i) \
+  do {                   \
+  } while (0)
+#endif
 
 struct GemmParams {
   int32_t M, K;                   // rows of A/C, reduction length
@@ -64,13 +83,15 @@ struct GemmCfg {
   static constexpr int kBBytes = BN * kKBytes;                    // BN * 128 B
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBNOut = SWIGLU ? BN / 2 : BN;             // output columns / tile
-  static constexpr int kTmemCols = 2 * BN;                        // double-buffered acc
+  // double-buffered accumulator; allocations are powers of two columns
+  static constexpr int kTmemCols = 2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512);
   static constexpr int kMNChunk = kKBytes / kElem;                // MN elems per 128 B
-  static constexpr int smem_bytes(int stages) { return stages * kStageBytes + 1024 /*align*/ + 256 /*bars*/; }
+  static constexpr int smem_bytes(int stages) { return stages * kStageBytes + 1024 /*align*/ + kBarBytes + kStageOutBytes; }
   static constexpr uint32_t kIdesc = make_idesc(KIND, B_MN, kBM, BN);
   static constexpr uint32_t kIdescHalf = make_idesc(KIND, B_MN, kBM, BN / 2);  // SWIGLU halves
   static constexpr int kPartBytes = kBM * (BN + 4) * 4;  // split-K partial tile
-  static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+  static_assert(BN == 64 || BN == 96 || BN == 128 || BN == 192 || BN == 256, "BN");
+  static_assert(BN % 64 == 0 || !(B_MN || SWIGLU), "BN 96 / 192: W[N,K] only; SWIGLU needs BN / 2 % 32 == 0");
   static_assert(!(SWIGLU && B_MN), "SWIGLU needs the W[N,K] layout");
   static_assert(kTmemCols >= 32 && kTmemCols <= 512, "TMEM columns");
 };
@@ -118,6 +139,58 @@ __device__ __forceinline__ void raise_abort(volatile int *abort_flag, int32_t *e
   if (err != nullptr) atomicExch(err, code);
 }
 
+// Epilogue of one accumulator row (TMEM lane quarter row, every other
+// 32-column chunk from c0): TMEM -> registers -> fused epilogue -> global.
+// With 16-bit operands (e.pre16) the scale / bias / residual of each chunk
+// are loaded one chunk ahead, the first by epi_row_prefetch before the
+// accumulator wait, so their latency overlaps the previous chunk's math.
+template <bool SWIGLU>
+__device__ __forceinline__ void epi_row_prefetch(const EpiArgs &e, int m, int n0, Pre16 &pf) {
+  if (!SWIGLU && e.pre16 && n0 + 32 <= e.N) epi_prefetch16(e, m, n0, pf);
+}
+
+template <int BN, int BN_OUT, int KIND, bool SWIGLU>
+__device__ __forceinline__ void epi_row(const EpiArgs &e, uint32_t t_row, int m, int n_base, int c0,
+                                        Pre16 &pf, uint8_t *stg) {
+  const bool raw_int = (KIND == 2) && (e.c_dtype == HX_S32) && (e.epi == HX_EPI_NONE);
+  const bool pre = !SWIGLU && e.pre16;
+#pragma unroll 1
+  for (int c = c0; c < BN_OUT / 32; c += 2) {
+    uint32_t r[32], r2[32];
+    tmem_ld_32x32b_x32(t_row + c * 32, r);
+    if constexpr (SWIGLU) tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, r2);
+    const int n0 = n_base + c * 32;
+    Pre16 nx;
+    if (pre && c + 2 < BN_OUT / 32 && n0 + 96 <= e.N) epi_prefetch16(e, m, n0 + 64, nx);
+    tmem_ld_wait();
+    if (threadIdx.x == 64 && c < 8) HX_GEMM_STAMP(8 + c);
+    float v[32], up[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if constexpr (KIND == 2)
+        v[j] = static_cast<float>(static_cast<int32_t>(r[j]));
+      else
+        v[j] = __uint_as_float(r[j]);
+      if constexpr (SWIGLU)
+        up[j] = __uint_as_float(r2[j]);
+      else
+        up[j] = 0.f;
+    }
+    if (!raw_int) {
+      if (pre && n0 + 32 <= e.N)
+        epi_apply16(e, v, up, m, pf);
+      else
+        epi_transform32(e, v, up, m, n0);
+    }
+    if (e.c_vec_ok && n0 + 32 <= e.N)
+      epi_store32_staged(e, v, r, raw_int, m - static_cast<int>(threadIdx.x & 31), n0, stg);
+    else
+      epi_store32(e, v, r, raw_int, m, n0);
+    pf = nx;
+    if (threadIdx.x == 64 && c < 8) HX_GEMM_STAMP(9 + c);
+  }
+}
+
 template <int BN, int KIND, bool B_MN, bool SWIGLU>
 __global__ void __launch_bounds__(kThreads, 1)
     hx_gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -145,9 +218,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *drain_bar = tempty_bar + 2;       // [1]
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain_bar + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  uint8_t *stage_out = reinterpret_cast<uint8_t *>(full_bar) + kBarBytes;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) HX_GEMM_STAMP(0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -177,7 +252,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Prologue done: let the next kernel in the stream start its own, then
   // wait for the previous one before reading or writing global memory.
   grid_dep_launch_dependents();
+  if (threadIdx.x == 0) HX_GEMM_STAMP(1);
   grid_dep_wait();
+  if (threadIdx.x == 0) HX_GEMM_STAMP(2);
 
   // Split-K: the CTAs of a cluster share each tile; CTA `rank` streams stage
   // blocks [sb_begin, sb_end) of it.  Without split-K: the whole K range.
@@ -280,6 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t d_tmem = tmem_base + acc * BN;
       for (int sb = sb_begin; sb < sb_end; ++sb) {
         bool f = (lane == 0) ? mbar_wait(&full_bar[stage], phase, p.timeout, abort_flag) : true;
+        if (it == 0 && sb == sb_begin && lane == 0) HX_GEMM_STAMP(3);
         f = __shfl_sync(0xffffffffu, f, 0);
         if (!f) {
           if (lane == 0) raise_abort(abort_flag, p.err_flag, 3);
@@ -332,6 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       if (lane == 0) umma_commit(&tfull_bar[acc]);  // accumulator ready
+      if (it == 0 && lane == 0) HX_GEMM_STAMP(4);
       __syncwarp();
     }
     if (!ok && lane == 0 && any_mma) {
@@ -350,14 +429,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       tile_coords(t, p, m_blk, n_blk);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
+      const int m = m_blk * kBM + row_in_tile;
+      const int c0 = (warp - 2) / 4;
+      Pre16 pf;
+      if (S == 1) epi_row_prefetch<SWIGLU>(p.epi, m, n_blk * Cfg::kBNOut + c0 * 32, pf);
       bool w = (lane == 0) ? mbar_wait(&tfull_bar[acc], acc_phase, p.timeout, abort_flag) : true;
       w = __shfl_sync(0xffffffffu, w, 0);
       if (!w) {
         if (lane == 0) raise_abort(abort_flag, p.err_flag, 4);
         break;
       }
+      if (it == 0 && warp == 2 && lane == 0) HX_GEMM_STAMP(5);
       tc_fence_after();
-      const int m = m_blk * kBM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
       if (S > 1) {
         // Split-K: park this CTA's partial accumulator (all BN columns, raw
@@ -379,33 +462,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
         continue;
       }
-#pragma unroll 1
-      for (int c = (warp - 2) / 4; c < Cfg::kBNOut / 32; c += 2) {
-        uint32_t r[32];
-        uint32_t r2[32];
-        tmem_ld_32x32b_x32(t_row + c * 32, r);
-        if constexpr (SWIGLU) tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, r2);
-        tmem_ld_wait();
-        float v[32], up[32];
-        const int n0 = n_blk * Cfg::kBNOut + c * 32;
-        const bool raw_int = (KIND == 2) && (p.epi.c_dtype == HX_S32) && (p.epi.epi == HX_EPI_NONE);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if constexpr (KIND == 2)
-            v[j] = static_cast<float>(static_cast<int32_t>(r[j]));
-          else
-            v[j] = __uint_as_float(r[j]);
-          if constexpr (SWIGLU)
-            up[j] = __uint_as_float(r2[j]);
-          else
-            up[j] = 0.f;
-        }
-        if (!raw_int) epi_transform32(p.epi, v, up, m, n0);
-        epi_store32(p.epi, v, r, raw_int, m, n0);
-      }
+      epi_row<BN, Cfg::kBNOut, KIND, SWIGLU>(p.epi, t_row, m, n_blk * Cfg::kBNOut, c0, pf,
+                                             stage_out + (warp - 2) * 4096);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if (it == 0 && warp == 2 && lane == 0) HX_GEMM_STAMP(6);
     }
   }
 
@@ -464,7 +526,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const int n0 = n_blk * Cfg::kBNOut + oc * 32;
           if (!raw_int) epi_transform32(p.epi, v, up, m, n0);
-          epi_store32(p.epi, v, r, raw_int, m, n0);
+          if (p.epi.c_vec_ok && n0 + 32 <= p.epi.N)
+            epi_store32_staged(p.epi, v, r, raw_int, m - lane, n0, stage_out + (warp - 2) * 4096);
+          else
+            epi_store32(p.epi, v, r, raw_int, m, n0);
         }
       }
     }
@@ -472,6 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  if (threadIdx.x == 0) HX_GEMM_STAMP(7);
 }
 
 }  // namespace hx

@@ -112,6 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *drain_bar = tempty_bar + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain_bar + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  uint8_t *stage_out = reinterpret_cast<uint8_t *>(full_bar) + kBarBytes;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = gemm_cluster_rank();   // 0 = leader
@@ -264,6 +265,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tile_coords(t, p, m_blk, n_blk);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
+      const int m = m_blk * (2 * kBM) + static_cast<int>(rank) * kBM + row_in_tile;
+      const int c0 = (warp - 2) / 4;
+      Pre16 pf;
+      epi_row_prefetch<SWIGLU>(p.epi, m, n_blk * kBNOut + c0 * 32, pf);
       bool w = (lane == 0) ? mbar_wait(&tfull_bar[acc], acc_phase, p.timeout, abort_flag) : true;
       w = __shfl_sync(0xffffffffu, w, 0);
       if (!w) {
@@ -271,31 +276,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int m = m_blk * (2 * kBM) + static_cast<int>(rank) * kBM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-#pragma unroll 1
-      for (int c = (warp - 2) / 4; c < kBNOut / 32; c += 2) {
-        uint32_t r[32], r2[32];
-        tmem_ld_32x32b_x32(t_row + c * 32, r);
-        if constexpr (SWIGLU) tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, r2);
-        tmem_ld_wait();
-        float v[32], up[32];
-        const int n0 = n_blk * kBNOut + c * 32;
-        const bool raw_int = (KIND == 2) && (p.epi.c_dtype == HX_S32) && (p.epi.epi == HX_EPI_NONE);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if constexpr (KIND == 2)
-            v[j] = static_cast<float>(static_cast<int32_t>(r[j]));
-          else
-            v[j] = __uint_as_float(r[j]);
-          if constexpr (SWIGLU)
-            up[j] = __uint_as_float(r2[j]);
-          else
-            up[j] = 0.f;
-        }
-        if (!raw_int) epi_transform32(p.epi, v, up, m, n0);
-        epi_store32(p.epi, v, r, raw_int, m, n0);
-      }
+      epi_row<BN, kBNOut, KIND, SWIGLU>(p.epi, t_row, m, n_blk * kBNOut, c0, pf,
+                                        stage_out + (warp - 2) * 4096);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {

@@ -196,7 +196,7 @@ int launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
   using Cfg = GemmCfg<BN, KIND, BMN, SW>;
   auto kern = hx_gemm_sm100_kernel<BN, KIND, BMN, SW>;
   const int ring = p.stages * p.kbs * Cfg::kStageBytes;
-  const int smem = std::max(ring, p.splits > 1 ? Cfg::kPartBytes : 0) + 1024 + 256;
+  const int smem = std::max(ring, p.splits > 1 ? Cfg::kPartBytes : 0) + 1024 + kBarBytes + kStageOutBytes;
   if (smem > kMaxDynSmem) return unsupported("shared memory for this tile plan exceeds 227 KB");
   static std::atomic<int> configured{0};
   if (configured.load(std::memory_order_acquire) < smem) {
@@ -245,7 +245,7 @@ int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &
                 cudaStream_t s) {
   auto kern = hx_gemm_sm100_2sm_kernel<BN, KIND, SW>;
   const int stage = p.kbs * (kBM * kKBytes + (BN / 2) * kKBytes);
-  const int smem = p.stages * stage + 1024 + 256;
+  const int smem = p.stages * stage + 1024 + kBarBytes + kStageOutBytes;
   if (smem > kMaxDynSmem) return unsupported("shared memory for this pair plan exceeds 227 KB");
   static std::atomic<int> configured{0};
   if (!configured.load(std::memory_order_acquire)) {
@@ -289,7 +289,13 @@ int dispatch_bn(int bn, const CUtensorMap &ta, const CUtensorMap &tb, const Gemm
     case 64:
       if constexpr (!(BMN && KIND == 2)) return launch_tc<64, KIND, BMN, SW>(ta, tb, p, grid, s);
       return unsupported("tile_n 64 with int8 B[K,N]");
+    case 96:
+      if constexpr (!BMN && !SW) return launch_tc<96, KIND, BMN, SW>(ta, tb, p, grid, s);
+      return unsupported("tile_n 96 with B[K,N] or SWIGLU");
     case 128: return launch_tc<128, KIND, BMN, SW>(ta, tb, p, grid, s);
+    case 192:
+      if constexpr (!BMN) return launch_tc<192, KIND, BMN, SW>(ta, tb, p, grid, s);
+      return unsupported("tile_n 192 with B[K,N]");
     case 256: return launch_tc<256, KIND, BMN, SW>(ta, tb, p, grid, s);
     default: return unsupported("tile_n");
   }
@@ -323,9 +329,10 @@ void plan_tiles(int64_t M, int64_t N, int64_t K, int ez, bool swiglu, bool bmn, 
   const double flop_per_us_sm = 10.9e6 * (ez == 1 ? 2.0 : 1.0);
   double best = 1e300;
   int best_bn = bn ? bn : 128, best_s = 1;
-  for (int b : {256, 128, 64}) {
+  for (int b : {256, 192, 128, 96, 64}) {
     if (bn && b != bn) continue;
     if (bmn && ez == 1 && b < 128) continue;
+    if ((b == 96 || b == 192) && (bmn || (swiglu && b == 96))) continue;
     const int out_w = swiglu ? b / 2 : b;
     const int64_t tiles = m_tiles * ((N + out_w - 1) / out_w);
     for (int sp : {1, 2, 3, 4, 6, 8}) {
@@ -426,6 +433,14 @@ EpiArgs make_epi(const hx_gemm_desc *d) {
   e.r_vec_ok = d->residual && aligned16(d->residual) && ((d->ldr * cz) % 16 == 0);
   e.b_vec_ok = d->bias && aligned16(d->bias);
   e.s_vec_ok = d->scale && aligned16(d->scale);
+  auto is16 = [](int t) { return t == HX_F16 || t == HX_BF16; };
+  const int epi = d->epilogue;
+  const bool uses_scale = (epi == HX_EPI_DEQUANT_SCALE);
+  const bool uses_bias = d->bias && epi != HX_EPI_NONE && epi != HX_EPI_RESIDUAL && epi != HX_EPI_SWIGLU;
+  const bool uses_res = (epi == HX_EPI_BIAS_RESIDUAL || epi == HX_EPI_RESIDUAL);
+  e.pre16 = (!uses_scale || (is16(d->scale_dtype) && e.s_vec_ok)) &&
+            (!uses_bias || (is16(d->bias_dtype) && e.b_vec_ok)) &&
+            (!uses_res || (is16(d->c_dtype) && e.r_vec_ok));
   return e;
 }
 
@@ -482,8 +497,11 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
   if (bn == 0 || d->split_k == 0) {
     plan_tiles(d->M, d->N, d->K, ez, swiglu, bmn, sms, bn, splits, d->split_k);
   }
-  if (bn != 64 && bn != 128 && bn != 256) return arg_fail("tile_n must be 64, 128 or 256");
+  if (bn != 64 && bn != 96 && bn != 128 && bn != 192 && bn != 256)
+    return arg_fail("tile_n must be 64, 96, 128, 192 or 256");
   if (bmn && ez == 1 && bn < 128) return unsupported("tile_n 64 with int8 B[K,N]");
+  if (bn == 96 && swiglu) return unsupported("tile_n 96 with SWIGLU");
+  if ((bn == 96 || bn == 192) && bmn) return unsupported("tile_n 96 / 192 with B[K,N]");
   // Several 128-byte K blocks per TMA instruction when K is whole blocks:
   // the per-instruction cost of TMA, not bytes, limits small boxes.
   const bool use3d = !bmn && (d->K * ez) % kKBytes == 0;
@@ -499,10 +517,14 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
     if (pair) bn = 256;
   }
   // Narrow tiles gain most (their boxes are smallest); wide tiles keep depth.
-  int kbs = !use3d ? 1 : (bn == 64 ? 4 : (bn == 128 ? 2 : (pair ? 2 : 1)));
+  int kbs = !use3d ? 1 : (bn == 64 ? 4 : 2);
+  if (const char *env = std::getenv("HX_GEMM_KBS"))  // tuning switch
+    if (use3d) kbs = std::max(1, std::min(4, std::atoi(env)));
   int stages = d->stages;
   const int per_stage = pair ? kBM * kKBytes + (bn / 2) * kKBytes : stage_bytes(bn);
-  auto fit = [&](int kb) { return std::min(8, (kMaxDynSmem - 1280) / (kb * per_stage)); };
+  auto fit = [&](int kb) {
+    return std::min(8, (kMaxDynSmem - 1024 - kBarBytes - kStageOutBytes) / (kb * per_stage));
+  };
   // an explicit stage count takes precedence: fewer K blocks per load until it fits
   while (kbs > 1 && fit(kbs) < std::max(2, stages)) kbs >>= 1;
   const int max_stages = fit(kbs);
@@ -912,7 +934,6 @@ int gemv_grouped_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32_t 
   cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int32_t) * count, s);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(counters)");
   const int grid = static_cast<int>(std::min<int64_t>(items, 2 * sms));  // two CTAs per SM
-  const int mc = M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8));
   const size_t smem =
       kGroupSlots * kGroupSlotBytes + 16 * kGroupSlots + 64;
   auto launch = [&](auto kern) -> cudaError_t {

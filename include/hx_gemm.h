@@ -96,7 +96,8 @@ typedef struct hx_gemm_desc {
   const void *scale;       /* [N] per-output-channel scale, or NULL           */
   /* Tile override (0 = choose automatically), the analogue of the
      reference's HexagonOptions.tileSizes (backend/hexagon_options.py:75).
-     tile_n in {64,128,256}; stages in [2,8]. */
+     tile_n in {64,96,128,192,256} (96 and 192: B_NK only, 96 not with
+     SWIGLU); stages in [2,8]. */
   int32_t tile_n;
   int32_t stages;
   int32_t max_ctas;        /* cap on persistent CTAs (0 = one per SM)         */

@@ -170,6 +170,36 @@ def test_tile_overrides(cuda_device, tile_n, epilogue):
     run_and_check(384, 520, 256, torch.float16, epilogue, tile_n=tile_n, seed=5)
 
 
+@pytest.mark.parametrize("tile_n", [96, 192])
+@pytest.mark.parametrize("epilogue", ["none", "bias_gelu_tanh", "bias_residual"])
+def test_tile_n_not_pow2(cuda_device, tile_n, epilogue):
+    """96- and 192-column tiles (TMEM allocation rounded up to a power of two)."""
+    run_and_check(384, 520, 256, torch.float16, epilogue, tile_n=tile_n, seed=15)
+    run_and_check(1000, 3 * tile_n + 17, 768, torch.bfloat16, epilogue, tile_n=tile_n, seed=16)
+
+
+def test_tile_n_192_swiglu_and_int8(cuda_device):
+    run_and_check(256, 400, 384, torch.bfloat16, "swiglu", tile_n=192, seed=17)
+    q = hx()
+    g = torch.Generator().manual_seed(18)
+    a = torch.randint(-127, 128, (300, 512), generator=g, dtype=torch.int64).to(torch.int8)
+    w = torch.randint(-127, 128, (500, 512), generator=g, dtype=torch.int64).to(torch.int8)
+    for tn in (96, 192):
+        out = q.gemm(a.cuda(), w.cuda(), tile_n=tn)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.cpu().numpy(), O.int8_gemm_exact(a.numpy(), w.numpy()))
+
+
+def test_tile_n_rejected_combinations(cuda_device):
+    q = hx()
+    from qcom_hexagon_backend._lib import HexagonB200Error
+    a = torch.randn(128, 128, device="cuda").half()
+    with pytest.raises((ValueError, HexagonB200Error)):
+        q.gemm(a, torch.randn(128, 256, device="cuda").half(), b_layout="kn", tile_n=96)
+    with pytest.raises((ValueError, HexagonB200Error)):
+        q.gemm(a, torch.randn(128, 128, device="cuda").half(), tile_n=100)
+
+
 @pytest.mark.parametrize("stages", [2, 3, 4])
 def test_stage_overrides(cuda_device, stages):
     run_and_check(512, 512, 1024, torch.bfloat16, "none", tile_n=256, stages=stages, seed=6)
@@ -375,7 +405,7 @@ def test_split_k_epilogues(cuda_device, split_k, epilogue):
 
 @pytest.mark.parametrize("shape", [(512, 384, 3072), (200, 300, 1000), (130, 520, 4096)],
                          ids=lambda s: "x".join(map(str, s)))
-@pytest.mark.parametrize("tile_n", [64, 128, 256])
+@pytest.mark.parametrize("tile_n", [64, 96, 128, 192, 256])
 def test_split_k_shapes(cuda_device, shape, tile_n):
     """K tails (2-D maps, one block per load), M/N tails, every tile width."""
     M, N, K = shape
