@@ -171,21 +171,58 @@ __device__ __forceinline__ void ld_raw16x32(const void *p, int64_t off, uint4 (&
 }
 
 __device__ __forceinline__ void raw16_to_f32(const uint4 (&w)[4], int dtype, float (&t)[32]) {
+  if (dtype == HX_F16) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t ws[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t ws[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      if (dtype == HX_F16) {
+      for (int h = 0; h < 4; ++h) {
         const __half2 x = *reinterpret_cast<const __half2 *>(&ws[h]);
         t[i * 8 + 2 * h] = __low2float(x);
         t[i * 8 + 2 * h + 1] = __high2float(x);
-      } else {  // bf16: the value is the upper half of an fp32
+      }
+    }
+  } else {  // bf16: the value is the upper half of an fp32
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t ws[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
         t[i * 8 + 2 * h] = __uint_as_float(ws[h] << 16);
         t[i * 8 + 2 * h + 1] = __uint_as_float(ws[h] & 0xffff0000u);
       }
     }
   }
+}
+
+// The residual chunk of a warp's 32 rows, loaded coalesced: lane l holds
+// rows i * 8 + l / 4 (i < 4), 16-byte column chunk l % 4 — whole 64-byte row
+// segments per instruction.  residual_to_rows() transposes it through the
+// warp's staging buffer to one row per lane.  Rows >= M read as zero.
+__device__ __forceinline__ void ld_residual_coalesced(const EpiArgs &e, int m, int n0, uint4 (&w)[4]) {
+  const int lane = threadIdx.x & 31;
+  const int m0 = m - lane;
+  const uint16_t *base = static_cast<const uint16_t *>(e.residual) + n0 + (lane & 3) * 8;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = i * 8 + (lane >> 2);
+    w[i] = (m0 + r < e.M) ? __ldcg(reinterpret_cast<const uint4 *>(base + static_cast<int64_t>(m0 + r) * e.ldr))
+                          : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+__device__ __forceinline__ void residual_to_rows(const uint4 (&w)[4], uint8_t *stg, uint4 (&row)[4]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = i * 8 + (lane >> 2), q = lane & 3;
+    *reinterpret_cast<uint4 *>(stg + r * 64 + ((q ^ ((r >> 1) & 3)) << 4)) = w[i];
+  }
+  __syncwarp();
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) row[q] = *reinterpret_cast<const uint4 *>(stg + lane * 64 + ((q ^ sw) << 4));
+  __syncwarp();  // stg is free again
 }
 
 // Valid when e.pre16 and n0 + 32 <= e.N.
@@ -199,42 +236,70 @@ __device__ __forceinline__ void epi_prefetch16(const EpiArgs &e, int m, int n0, 
     ld_raw16x32<false>(e.bias, n0, f.a);
   if (epi == HX_EPI_DEQUANT_SCALE && e.bias != nullptr)
     ld_raw16x32<false>(e.bias, n0, f.b);
-  else if (residual && m < e.M)
-    ld_raw16x32<true>(e.residual, static_cast<int64_t>(m) * e.ldr + n0, f.b);
+  else if (residual)
+    ld_residual_coalesced(e, m, n0, f.b);  // warp-collective
 }
 
-// epi_transform32 on prefetched operands.
-__device__ __forceinline__ void epi_apply16(const EpiArgs &e, float (&v)[32], const float (&up)[32],
-                                            int m, const Pre16 &f) {
-  const int epi = e.epi;
-  if (epi == HX_EPI_NONE) return;
-  if (epi == HX_EPI_SWIGLU) {
-    swiglu32(e, v, up);
-    return;
+// Compile-time specialised epilogue of one full 32-column chunk on
+// prefetched operands (valid when e.pre16): EPI is the epilogue, CT the
+// output dtype.  The hot loop instantiates exactly one of these, so its
+// instruction footprint holds only the path that runs.
+template <int EPI>
+__device__ __forceinline__ void epi_prefetch_t(const EpiArgs &e, int m, int n0, Pre16 &f) {
+  if constexpr (EPI == HX_EPI_DEQUANT_SCALE) {
+    ld_raw16x32<false>(e.scale, n0, f.a);
+    if (e.bias != nullptr) ld_raw16x32<false>(e.bias, n0, f.b);
+  } else if constexpr (EPI == HX_EPI_BIAS || EPI == HX_EPI_BIAS_GELU_TANH ||
+                       EPI == HX_EPI_BIAS_SILU || EPI == HX_EPI_BIAS_RESIDUAL) {
+    if (e.bias != nullptr) ld_raw16x32<false>(e.bias, n0, f.a);
   }
-  float t[32];
-  if (epi == HX_EPI_DEQUANT_SCALE) {
-    raw16_to_f32(f.a, e.scale_dtype, t);
+  if constexpr (EPI == HX_EPI_BIAS_RESIDUAL || EPI == HX_EPI_RESIDUAL) {
+    ld_residual_coalesced(e, m, n0, f.b);
+  }
+}
+
+template <int EPI, int CT>
+__device__ __forceinline__ void epi_apply_t(const EpiArgs &e, float (&v)[32], const float (&up)[32],
+                                            int m, const Pre16 &f, uint8_t *stg) {
+  constexpr bool kHw = (CT != HX_F32);  // hardware tanh for 16-bit outputs
+  if constexpr (EPI == HX_EPI_SWIGLU) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] *= t[j];
-    if (e.bias != nullptr) {
-      raw16_to_f32(f.b, e.bias_dtype, t);
+    for (int j = 0; j < 32; ++j) v[j] = (kHw ? silu_hw(v[j]) : silu(v[j])) * up[j];
+  } else if constexpr (EPI != HX_EPI_NONE) {
+    float t[32];
+    if constexpr (EPI == HX_EPI_DEQUANT_SCALE) {
+      raw16_to_f32(f.a, e.scale_dtype, t);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] += t[j];
+      for (int j = 0; j < 32; ++j) v[j] *= t[j];
+      if (e.bias != nullptr) {
+        raw16_to_f32(f.b, e.bias_dtype, t);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += t[j];
+      }
+    } else {
+      if constexpr (EPI != HX_EPI_RESIDUAL) {
+        if (e.bias != nullptr) {
+          raw16_to_f32(f.a, e.bias_dtype, t);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += t[j];
+        }
+      }
+      if constexpr (EPI == HX_EPI_BIAS_RESIDUAL || EPI == HX_EPI_RESIDUAL) {
+        uint4 rrow[4];
+        residual_to_rows(f.b, stg, rrow);
+        raw16_to_f32(rrow, CT, t);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += t[j];
+      }
+      if constexpr (EPI == HX_EPI_BIAS_GELU_TANH) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = kHw ? gelu_tanh_hw(v[j]) : gelu_tanh(v[j]);
+      } else if constexpr (EPI == HX_EPI_BIAS_SILU) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = kHw ? silu_hw(v[j]) : silu(v[j]);
+      }
     }
-    return;
   }
-  if (e.bias != nullptr && epi != HX_EPI_RESIDUAL) {
-    raw16_to_f32(f.a, e.bias_dtype, t);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] += t[j];
-  }
-  if ((epi == HX_EPI_BIAS_RESIDUAL || epi == HX_EPI_RESIDUAL) && m < e.M) {
-    raw16_to_f32(f.b, e.c_dtype, t);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] += t[j];
-  }
-  epi_activate32(e, v);
 }
 
 // Apply the epilogue to 32 consecutive output columns of one row.
@@ -360,22 +425,24 @@ __device__ __forceinline__ void epi_store_scalar(const EpiArgs &e, float v, int3
 }
 
 
-// epi_store32 for a whole warp through its 4 KB staging buffer `stg`: each
-// thread parks its row segment in shared memory, then the warp writes 8 rows
-// x 64 B (16-bit C) or 4 rows x 128 B (32-bit C) per store instruction
-// instead of 32 rows x 16 B, a quarter of the L1 store wavefronts.  The 16-byte
-// chunks of a row are XOR-swizzled by row so both shared-memory phases are
-// free of bank conflicts.  All 32 lanes must call it with the same n0 and
-// m0 = the warp's first row; requires e.c_vec_ok and n0 + 32 <= e.N.
-__device__ __forceinline__ void epi_store32_staged(const EpiArgs &e, const float (&v)[32],
-                                                   const uint32_t (&raw)[32], bool raw_int, int m0,
-                                                   int n0, uint8_t *stg) {
+// Store of one full 32-column chunk for a whole warp through its 4 KB
+// staging buffer `stg`: each thread parks its row segment in shared memory,
+// then the warp writes 8 rows x 64 B (16-bit C) or 4 rows x 128 B (32-bit C)
+// per store instruction instead of 32 rows x 16 B.  The 16-byte chunks of a
+// row are XOR-swizzled by row so both shared-memory phases are free of bank
+// conflicts.  All 32 lanes call it with the same n0 and m0 = the warp's first
+// row; requires e.c_vec_ok and n0 + 32 <= e.N.  RAW: v is ignored and the
+// int32 bits in raw are stored.
+template <int CT, bool RAW>
+__device__ __forceinline__ void epi_store32_staged_t(const EpiArgs &e, const float (&v)[32],
+                                                     const uint32_t (&raw)[32], int m0, int n0,
+                                                     uint8_t *stg) {
   const int lane = threadIdx.x & 31;
-  if (e.c_dtype == HX_F16 || e.c_dtype == HX_BF16) {
+  if constexpr (CT == HX_F16 || CT == HX_BF16) {
     uint32_t pk[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      if (e.c_dtype == HX_F16) {
+      if constexpr (CT == HX_F16) {
         __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
         pk[j] = *reinterpret_cast<uint32_t *>(&h);
       } else {
@@ -403,10 +470,12 @@ __device__ __forceinline__ void epi_store32_staged(const EpiArgs &e, const float
     uint32_t w[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      if (e.c_dtype == HX_F32)
+      if constexpr (RAW)
+        w[j] = raw[j];
+      else if constexpr (CT == HX_F32)
         w[j] = __float_as_uint(v[j]);
       else
-        w[j] = raw_int ? raw[j] : static_cast<uint32_t>(__float2int_rn(v[j]));
+        w[j] = static_cast<uint32_t>(__float2int_rn(v[j]));
     }
     uint8_t *row = stg + lane * 128;
     const int sw = lane & 7;

@@ -143,25 +143,26 @@ __device__ __forceinline__ void raise_abort(volatile int *abort_flag, int32_t *e
 // 32-column chunk from c0): TMEM -> registers -> fused epilogue -> global.
 // With 16-bit operands (e.pre16) the scale / bias / residual of each chunk
 // are loaded one chunk ahead, the first by epi_row_prefetch before the
-// accumulator wait, so their latency overlaps the previous chunk's math.
+// accumulator wait, so their latency overlaps the previous chunk's stores.
 template <bool SWIGLU>
 __device__ __forceinline__ void epi_row_prefetch(const EpiArgs &e, int m, int n0, Pre16 &pf) {
   if (!SWIGLU && e.pre16 && n0 + 32 <= e.N) epi_prefetch16(e, m, n0, pf);
 }
 
-template <int BN, int BN_OUT, int KIND, bool SWIGLU>
-__device__ __forceinline__ void epi_row(const EpiArgs &e, uint32_t t_row, int m, int n_base, int c0,
-                                        Pre16 &pf, uint8_t *stg) {
-  const bool raw_int = (KIND == 2) && (e.c_dtype == HX_S32) && (e.epi == HX_EPI_NONE);
-  const bool pre = !SWIGLU && e.pre16;
+// The loop for one (epilogue, output dtype) pair, fixed at compile time, for
+// rows whose chunks are all full and whose operands are 16-bit and aligned
+// (e.pre16, e.c_vec_ok): nothing in it calls out, so its registers stay put.
+template <int BN, int BN_OUT, int KIND, bool SWIGLU, int EPI, int CT>
+__device__ __forceinline__ void epi_row_t(const EpiArgs &e, uint32_t t_row, int m, int n_base, int c0,
+                                          Pre16 &pf, uint8_t *stg) {
+  constexpr bool kRaw = (KIND == 2) && (CT == HX_S32) && (EPI == HX_EPI_NONE);
+  constexpr bool kPre = !(EPI == HX_EPI_NONE || EPI == HX_EPI_SWIGLU);  // operands to prefetch
 #pragma unroll 1
   for (int c = c0; c < BN_OUT / 32; c += 2) {
     uint32_t r[32], r2[32];
     tmem_ld_32x32b_x32(t_row + c * 32, r);
     if constexpr (SWIGLU) tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, r2);
     const int n0 = n_base + c * 32;
-    Pre16 nx;
-    if (pre && c + 2 < BN_OUT / 32 && n0 + 96 <= e.N) epi_prefetch16(e, m, n0 + 64, nx);
     tmem_ld_wait();
     if (threadIdx.x == 64 && c < 8) HX_GEMM_STAMP(8 + c);
     float v[32], up[32];
@@ -176,18 +177,104 @@ __device__ __forceinline__ void epi_row(const EpiArgs &e, uint32_t t_row, int m,
       else
         up[j] = 0.f;
     }
-    if (!raw_int) {
-      if (pre && n0 + 32 <= e.N)
-        epi_apply16(e, v, up, m, pf);
-      else
-        epi_transform32(e, v, up, m, n0);
+    if constexpr (!kRaw) epi_apply_t<EPI, CT>(e, v, up, m, pf, stg);
+    // The next chunk's operands load while this chunk is stored.
+    if constexpr (kPre) {
+      if (c + 2 < BN_OUT / 32) epi_prefetch_t<EPI>(e, m, n0 + 64, pf);
     }
-    if (e.c_vec_ok && n0 + 32 <= e.N)
-      epi_store32_staged(e, v, r, raw_int, m - static_cast<int>(threadIdx.x & 31), n0, stg);
-    else
-      epi_store32(e, v, r, raw_int, m, n0);
-    pf = nx;
+    epi_store32_staged_t<CT, kRaw>(e, v, r, m - static_cast<int>(threadIdx.x & 31), n0, stg);
     if (threadIdx.x == 64 && c < 8) HX_GEMM_STAMP(9 + c);
+  }
+}
+
+// Every other row (a partial last tile, unaligned C, 32-bit operands): the
+// runtime-dispatched epilogue and row stores, out of line.
+template <int BN, int BN_OUT, int KIND, bool SWIGLU>
+__device__ __noinline__ void epi_row_generic(const EpiArgs &e, uint32_t t_row, int m, int n_base, int c0) {
+  const bool raw_int = (KIND == 2) && (e.c_dtype == HX_S32) && (e.epi == HX_EPI_NONE);
+#pragma unroll 1
+  for (int c = c0; c < BN_OUT / 32; c += 2) {
+    uint32_t r[32], r2[32];
+    tmem_ld_32x32b_x32(t_row + c * 32, r);
+    if constexpr (SWIGLU) tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, r2);
+    tmem_ld_wait();
+    float v[32], up[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if constexpr (KIND == 2)
+        v[j] = static_cast<float>(static_cast<int32_t>(r[j]));
+      else
+        v[j] = __uint_as_float(r[j]);
+      if constexpr (SWIGLU)
+        up[j] = __uint_as_float(r2[j]);
+      else
+        up[j] = 0.f;
+    }
+    const int n0 = n_base + c * 32;
+    if (!raw_int) epi_transform32(e, v, up, m, n0);
+    epi_store32(e, v, r, raw_int, m, n0);
+  }
+}
+
+template <int BN, int BN_OUT, int KIND, bool SWIGLU, int CT>
+__device__ __forceinline__ void epi_row_ct(const EpiArgs &e, uint32_t t_row, int m, int n_base, int c0,
+                                           Pre16 &pf, uint8_t *stg) {
+#define HX_EPI_ROW(E) epi_row_t<BN, BN_OUT, KIND, SWIGLU, E, CT>(e, t_row, m, n_base, c0, pf, stg)
+  if constexpr (SWIGLU) {
+    HX_EPI_ROW(HX_EPI_SWIGLU);
+  } else if constexpr (CT == HX_S32) {
+    HX_EPI_ROW(HX_EPI_NONE);  // int32 output: int8 inputs, no epilogue
+  } else {
+    switch (e.epi) {
+      case HX_EPI_NONE: HX_EPI_ROW(HX_EPI_NONE); break;
+      case HX_EPI_BIAS: HX_EPI_ROW(HX_EPI_BIAS); break;
+      case HX_EPI_BIAS_GELU_TANH: HX_EPI_ROW(HX_EPI_BIAS_GELU_TANH); break;
+      case HX_EPI_BIAS_RESIDUAL: HX_EPI_ROW(HX_EPI_BIAS_RESIDUAL); break;
+      case HX_EPI_RESIDUAL: HX_EPI_ROW(HX_EPI_RESIDUAL); break;
+      case HX_EPI_BIAS_SILU: HX_EPI_ROW(HX_EPI_BIAS_SILU); break;
+      case HX_EPI_DEQUANT_SCALE:
+        if constexpr (KIND == 2) HX_EPI_ROW(HX_EPI_DEQUANT_SCALE);
+        break;
+      default: break;
+    }
+  }
+#undef HX_EPI_ROW
+}
+
+// Epilogue of one accumulator row (TMEM lane quarter row, every other
+// 32-column chunk from c0): rows of full tiles with aligned 16-bit operands
+// dispatch once on the output dtype and the epilogue to a loop specialised
+// for that pair; the rest take the generic loop.
+template <int BN, int BN_OUT, int KIND, bool SWIGLU>
+__device__ __forceinline__ void epi_row(const EpiArgs &e, uint32_t t_row, int m, int n_base, int c0,
+                                        Pre16 &pf, uint8_t *stg) {
+  if (!(e.pre16 && e.c_vec_ok && n_base + BN_OUT <= e.N)) {
+    epi_row_generic<BN, BN_OUT, KIND, SWIGLU>(e, t_row, m, n_base, c0);
+    return;
+  }
+  switch (e.c_dtype) {
+    case HX_F16: epi_row_ct<BN, BN_OUT, KIND, SWIGLU, HX_F16>(e, t_row, m, n_base, c0, pf, stg); break;
+    case HX_BF16: epi_row_ct<BN, BN_OUT, KIND, SWIGLU, HX_BF16>(e, t_row, m, n_base, c0, pf, stg); break;
+    case HX_F32: epi_row_ct<BN, BN_OUT, KIND, SWIGLU, HX_F32>(e, t_row, m, n_base, c0, pf, stg); break;
+    case HX_S32:
+      if constexpr (KIND == 2 && !SWIGLU) epi_row_ct<BN, BN_OUT, KIND, SWIGLU, HX_S32>(e, t_row, m, n_base, c0, pf, stg);
+      break;
+    default: break;
+  }
+}
+
+// Runtime-dispatched staged store for the split-K reduction.
+__device__ __forceinline__ void epi_store32_staged_rt(const EpiArgs &e, const float (&v)[32],
+                                                      const uint32_t (&raw)[32], bool raw_int, int m0,
+                                                      int n0, uint8_t *stg) {
+  switch (e.c_dtype) {
+    case HX_F16: epi_store32_staged_t<HX_F16, false>(e, v, raw, m0, n0, stg); break;
+    case HX_BF16: epi_store32_staged_t<HX_BF16, false>(e, v, raw, m0, n0, stg); break;
+    case HX_F32: epi_store32_staged_t<HX_F32, false>(e, v, raw, m0, n0, stg); break;
+    default:
+      if (raw_int) epi_store32_staged_t<HX_S32, true>(e, v, raw, m0, n0, stg);
+      else epi_store32_staged_t<HX_S32, false>(e, v, raw, m0, n0, stg);
+      break;
   }
 }
 
@@ -460,6 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        if (it == 0 && warp == 2 && lane == 0) HX_GEMM_STAMP(6);
         continue;
       }
       epi_row<BN, Cfg::kBNOut, KIND, SWIGLU>(p.epi, t_row, m, n_blk * Cfg::kBNOut, c0, pf,
@@ -479,7 +567,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Every CTA's partial is in its smem; each reduces the output column
     // chunks it owns (chunk oc belongs to rank oc % S) over the S partials
     // through distributed shared memory, applies the epilogue once, stores.
+    if (threadIdx.x == 0) HX_GEMM_STAMP(12);
     gemm_cluster_sync();
+    if (threadIdx.x == 64) HX_GEMM_STAMP(13);
     if (warp >= 2) {
       const int q = warp & 3;
       const int row_in_tile = q * 32 + lane;
@@ -527,13 +617,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int n0 = n_blk * Cfg::kBNOut + oc * 32;
           if (!raw_int) epi_transform32(p.epi, v, up, m, n0);
           if (p.epi.c_vec_ok && n0 + 32 <= p.epi.N)
-            epi_store32_staged(p.epi, v, r, raw_int, m - lane, n0, stage_out + (warp - 2) * 4096);
+            epi_store32_staged_rt(p.epi, v, r, raw_int, m - lane, n0, stage_out + (warp - 2) * 4096);
           else
             epi_store32(p.epi, v, r, raw_int, m, n0);
         }
       }
     }
+    if (threadIdx.x == 64) HX_GEMM_STAMP(14);
     gemm_cluster_sync();  // peers keep their smem until every CTA has read it
+    if (threadIdx.x == 64) HX_GEMM_STAMP(15);
   }
 
   if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);

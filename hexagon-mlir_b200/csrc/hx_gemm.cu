@@ -20,9 +20,9 @@
 #include <utility>
 
 #include "gemm_chain.cuh"
+#include "launch.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_sm100.cuh"
-#include "gemm_sm100_2sm.cuh"
 #include "gemv_grouped.cuh"
 #include "gemv_w8a16.cuh"
 #include "w8a16_sm100.cuh"
@@ -31,22 +31,9 @@
 #define HX_VERSION 1
 
 namespace hx {
+thread_local std::string g_last_error;
 namespace {
 
-thread_local std::string g_last_error;
-
-int cuda_fail(cudaError_t e, const char *where) {
-  g_last_error = std::string(where) + ": " + cudaGetErrorString(e);
-  return HX_E_CUDA;
-}
-int arg_fail(const char *why) {
-  g_last_error = why;
-  return HX_E_INVALID_ARG;
-}
-int unsupported(const char *why) {
-  g_last_error = why;
-  return HX_E_UNSUPPORTED;
-}
 
 // ------------------------------------------------------------ device cache
 struct DeviceInfo {
@@ -166,152 +153,10 @@ int esize(int dtype) {
 }
 __host__ __device__ inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in limit per block on sm_100
-constexpr int kNeedsNoSplit = 1;     // internal: split-K clusters would not all be resident
-constexpr uint64_t kDefaultTimeout = 4000000000ull;  // ~2 s at 2 GHz
 
 // ------------------------------------------------------------ launch
-// Launch with programmatic stream serialization (PDL): the kernel may begin
-// while its predecessor finishes; it calls griddepcontrol.wait before its
-// first global-memory access, so ordering is unchanged.
-template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
-                       Args &&...args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
-}
-
-template <int BN, int KIND, bool BMN, bool SW>
-int launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p, int grid,
-              cudaStream_t s) {
-  using Cfg = GemmCfg<BN, KIND, BMN, SW>;
-  auto kern = hx_gemm_sm100_kernel<BN, KIND, BMN, SW>;
-  const int ring = p.stages * p.kbs * Cfg::kStageBytes;
-  const int smem = std::max(ring, p.splits > 1 ? Cfg::kPartBytes : 0) + 1024 + kBarBytes + kStageOutBytes;
-  if (smem > kMaxDynSmem) return unsupported("shared memory for this tile plan exceeds 227 KB");
-  static std::atomic<int> configured{0};
-  if (configured.load(std::memory_order_acquire) < smem) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kMaxDynSmem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-    configured.store(kMaxDynSmem, std::memory_order_release);
-  }
-  cudaError_t e;
-  if (p.splits > 1) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = p.splits;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    // Split-K needs every cluster resident at once (one tile per cluster).
-    static std::atomic<int> max_clusters[9];
-    int mc = max_clusters[p.splits].load(std::memory_order_acquire);
-    if (mc == 0) {
-      e = cudaOccupancyMaxActiveClusters(&mc, kern, &cfg);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
-      max_clusters[p.splits].store(std::max(mc, 1), std::memory_order_release);
-    }
-    if (grid / p.splits > mc) return kNeedsNoSplit;
-    cfg.numAttrs = 2;
-    e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
-  } else {
-    e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, ta, tb, p);
-  }
-  if (e == cudaSuccess) e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "hx_gemm_sm100_kernel launch");
-  return HX_OK;
-}
-
-template <int BN, int KIND, bool SW>
-int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p, int grid,
-                cudaStream_t s) {
-  auto kern = hx_gemm_sm100_2sm_kernel<BN, KIND, SW>;
-  const int stage = p.kbs * (kBM * kKBytes + (BN / 2) * kKBytes);
-  const int smem = p.stages * stage + 1024 + kBarBytes + kStageOutBytes;
-  if (smem > kMaxDynSmem) return unsupported("shared memory for this pair plan exceeds 227 KB");
-  static std::atomic<int> configured{0};
-  if (!configured.load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pair)");
-    configured.store(1, std::memory_order_release);
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
-  if (e == cudaSuccess) e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "hx_gemm_sm100_2sm_kernel launch");
-  return HX_OK;
-}
-
-int dispatch_pair(int kind, int bn, bool sw, const CUtensorMap &ta, const CUtensorMap &tb,
-                  const GemmParams &p, int grid, cudaStream_t s) {
-  if (bn != 256) return unsupported("pair tiles use tile_n 256");
-  if (kind == 0) return sw ? launch_pair<256, 0, true>(ta, tb, p, grid, s) : launch_pair<256, 0, false>(ta, tb, p, grid, s);
-  if (kind == 1) return sw ? launch_pair<256, 1, true>(ta, tb, p, grid, s) : launch_pair<256, 1, false>(ta, tb, p, grid, s);
-  if (sw) return unsupported("SWIGLU with int8 inputs");
-  return launch_pair<256, 2, false>(ta, tb, p, grid, s);
-}
-
-template <int KIND, bool BMN, bool SW>
-int dispatch_bn(int bn, const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
-                int grid, cudaStream_t s) {
-  switch (bn) {
-    case 64:
-      if constexpr (!(BMN && KIND == 2)) return launch_tc<64, KIND, BMN, SW>(ta, tb, p, grid, s);
-      return unsupported("tile_n 64 with int8 B[K,N]");
-    case 96:
-      if constexpr (!BMN && !SW) return launch_tc<96, KIND, BMN, SW>(ta, tb, p, grid, s);
-      return unsupported("tile_n 96 with B[K,N] or SWIGLU");
-    case 128: return launch_tc<128, KIND, BMN, SW>(ta, tb, p, grid, s);
-    case 192:
-      if constexpr (!BMN) return launch_tc<192, KIND, BMN, SW>(ta, tb, p, grid, s);
-      return unsupported("tile_n 192 with B[K,N]");
-    case 256: return launch_tc<256, KIND, BMN, SW>(ta, tb, p, grid, s);
-    default: return unsupported("tile_n");
-  }
-}
-
-template <int KIND>
-int dispatch_kind(int bn, bool bmn, bool sw, const CUtensorMap &ta, const CUtensorMap &tb,
-                  const GemmParams &p, int grid, cudaStream_t s) {
-  if (bmn) return dispatch_bn<KIND, true, false>(bn, ta, tb, p, grid, s);
-  if (sw) {
-    if constexpr (KIND == 2) return unsupported("SWIGLU with int8 inputs");
-    else return dispatch_bn<KIND, false, true>(bn, ta, tb, p, grid, s);
-  }
-  return dispatch_bn<KIND, false, false>(bn, ta, tb, p, grid, s);
-}
-
+// launch_pdl and the tile-GEMM launchers live in launch.cuh; the kernels are
+// instantiated per input kind in gemm_kind{0,1,2}.cu (compiled in parallel).
 int stage_bytes(int bn) { return kBM * kKBytes + bn * kKBytes; }
 
 // Tile plan: width BN (and, only when the caller asks, a split-K factor S).
@@ -592,7 +437,11 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
   };
   if (pair) {
     const int pairs = static_cast<int>(std::min<int64_t>(total, sms / 2));
-    return dispatch_pair(kind, bn, swiglu, ta, tb, p, 2 * pairs, s);
+    switch (kind) {
+      case 0: return dispatch_pair_kind<0>(bn, swiglu, ta, tb, p, 2 * pairs, s);
+      case 1: return dispatch_pair_kind<1>(bn, swiglu, ta, tb, p, 2 * pairs, s);
+      default: return dispatch_pair_kind<2>(bn, swiglu, ta, tb, p, 2 * pairs, s);
+    }
   }
   int r = dispatch();
   if (r == kNeedsNoSplit) {  // clusters would not all fit at once: run unsplit
