@@ -71,6 +71,8 @@ struct GemmParams {
   int32_t splits;                 // split-K: CTAs per cluster sharing one tile (1 = none)
   uint64_t timeout;               // cycles per bounded wait
   int32_t *err_flag;              // optional global error word
+  uint4 *ws;                      // split-K: [tile][rank][BN/32][8][128] x 16 B of partials
+  int32_t red_smem;               // split-K: fetch remote partials into the ring (else read L2)
   EpiArgs epi;
 };
 
@@ -88,8 +90,11 @@ struct GemmCfg {
   static constexpr int kMNChunk = kKBytes / kElem;                // MN elems per 128 B
   static constexpr int smem_bytes(int stages) { return stages * kStageBytes + 1024 /*align*/ + kBarBytes + kStageOutBytes; }
   static constexpr uint32_t kIdesc = make_idesc(KIND, B_MN, kBM, BN);
+  // split-K: ring bytes that receive the remote partials of a rank's chunks
+  __host__ __device__ static constexpr int red_bytes(int splits) {
+    return ((kBNOut / 32 + splits - 1) / splits) * (splits - 1) * (SWIGLU ? 2 : 1) * 8 * kBM * 16;
+  }
   static constexpr uint32_t kIdescHalf = make_idesc(KIND, B_MN, kBM, BN / 2);  // SWIGLU halves
-  static constexpr int kPartBytes = kBM * (BN + 4) * 4;  // split-K partial tile
   static_assert(BN == 64 || BN == 96 || BN == 128 || BN == 192 || BN == 256, "BN");
   static_assert(BN % 64 == 0 || !(B_MN || SWIGLU), "BN 96 / 192: W[N,K] only; SWIGLU needs BN / 2 % 32 == 0");
   static_assert(!(SWIGLU && B_MN), "SWIGLU needs the W[N,K] layout");
@@ -124,14 +129,6 @@ __device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t addr) {
   uint32_t v;
   asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
   return v;
-}
-
-__device__ __forceinline__ void ld_cluster_v4(uint32_t addr, uint32_t &a, uint32_t &b, uint32_t &c,
-                                              uint32_t &d) {
-  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
-               : "r"(addr)
-               : "memory");
 }
 
 __device__ __forceinline__ void raise_abort(volatile int *abort_flag, int32_t *err, int code) {
@@ -293,17 +290,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int B_ST = p.kbs * Cfg::kBBytes;  // bytes of B per stage
   uint8_t *sA = smem;
   uint8_t *sB = smem + STAGES * A_ST;
-  // Split-K parks a [128][BN + 4] fp32 partial over the ring: the barriers
-  // go after whichever of the two is larger.
+  // Split-K lands remote partials in the ring once the mainloop is done: the
+  // barriers go after whichever of the two is larger.
   const int ring_bytes = STAGES * (A_ST + B_ST);
-  const int part_bytes = p.splits > 1 ? Cfg::kPartBytes : 0;
-  uint64_t *full_bar =
-      reinterpret_cast<uint64_t *>(smem + (ring_bytes > part_bytes ? ring_bytes : part_bytes));
+  const int red_bytes = (p.splits > 1 && p.red_smem) ? Cfg::red_bytes(p.splits) : 0;
+  uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + (ring_bytes > red_bytes ? ring_bytes : red_bytes));
   uint64_t *empty_bar = full_bar + STAGES;
   uint64_t *tfull_bar = empty_bar + STAGES;   // [2]
   uint64_t *tempty_bar = tfull_bar + 2;       // [2]
   uint64_t *drain_bar = tempty_bar + 2;       // [1]
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain_bar + 1);
+  uint64_t *red_bar = drain_bar + 1;          // [1] split-K: remote partials landed
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(red_bar + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   uint8_t *stage_out = reinterpret_cast<uint8_t *>(full_bar) + kBarBytes;
 
@@ -321,6 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty_bar[a], kEpiWarps);
     }
     mbar_init(drain_bar, 1);
+    mbar_init(red_bar, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -530,23 +528,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
       if (S > 1) {
-        // Split-K: park this CTA's partial accumulator (all BN columns, raw
-        // fp32 / int32 bits) in its own smem, row-major [128][BN + 4] (the pad
-        // spreads rows over banks); the stage ring is idle once the tile's
-        // last UMMA has completed.
-        uint32_t *part = reinterpret_cast<uint32_t *>(smem) + row_in_tile * (BN + 4);
+        // Split-K: write the partial columns that other ranks own to this
+        // CTA's slot of the L2 workspace (raw fp32 / int32 bits), laid out
+        // [column chunk][4-column group][row] in 16-byte units so a warp's 32
+        // rows fill 512 contiguous bytes.  Chunks this rank owns stay in TMEM
+        // (one tile per cluster: the accumulator is not released).
+        uint4 *slot = p.ws + (static_cast<size_t>(t) * S + rank) * (BN / 32) * 8 * kBM;
 #pragma unroll 1
         for (int c = (warp - 2) / 4; c < BN / 32; c += 2) {
+          if ((c % (Cfg::kBNOut / 32)) % S == static_cast<int>(rank)) continue;
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + c * 32, r);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<uint4 *>(part + c * 32 + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+          for (int g = 0; g < 8; ++g)
+            slot[(c * 8 + g) * kBM + row_in_tile] = make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
         if (it == 0 && warp == 2 && lane == 0) HX_GEMM_STAMP(6);
         continue;
       }
@@ -564,55 +561,135 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
 
   if (S > 1) {
-    // Every CTA's partial is in its smem; each reduces the output column
-    // chunks it owns (chunk oc belongs to rank oc % S) over the S partials
-    // through distributed shared memory, applies the epilogue once, stores.
+    // Every CTA's non-owned partials are in the workspace (the cluster
+    // barrier's release / acquire makes them visible).  Each CTA fetches the
+    // partials of the output chunks it owns (chunk oc belongs to rank oc % S)
+    // into its idle stage ring with 16 KB bulk copies, then reduces them in
+    // rank order — its own straight from TMEM — applies the epilogue once and
+    // stores.  Ring slot of (owned chunk j, remote rank index ri, half h):
+    // ((j * (S - 1) + ri) * H + h) * 16 KB, H = 2 for SWIGLU (gate, up).
+    constexpr int kH = SWIGLU ? 2 : 1;
+    constexpr int kChunkBytes = 8 * kBM * 16;
+    constexpr int kUpChunk = Cfg::kBNOut / 32;  // SWIGLU: up half starts here
+    const int n_own = (Cfg::kBNOut / 32 - static_cast<int>(rank) + S - 1) / S;
     if (threadIdx.x == 0) HX_GEMM_STAMP(12);
     gemm_cluster_sync();
     if (threadIdx.x == 64) HX_GEMM_STAMP(13);
+    const bool via_smem = p.red_smem != 0;
+    if (threadIdx.x == 64 && via_smem) {
+      asm volatile("fence.proxy.async.global;" ::: "memory");  // generic writes -> bulk reads
+      const uint32_t bytes = static_cast<uint32_t>(n_own * (S - 1) * kH * kChunkBytes);
+      if (bytes > 0) {
+        mbar_arrive_expect_tx(red_bar, bytes);
+        for (int t = t_first; t < p.total_tiles; t += t_step) {  // one tile per cluster
+          for (int j = 0; j < n_own; ++j) {
+            const int oc = static_cast<int>(rank) + j * S;
+            int ri = 0;
+            for (int rr = 0; rr < S; ++rr) {
+              if (rr == static_cast<int>(rank)) continue;
+              const uint4 *src = p.ws + (static_cast<size_t>(t) * S + rr) * (BN / 32) * 8 * kBM;
+              for (int h = 0; h < kH; ++h)
+                bulk_load_1d(smem + ((j * (S - 1) + ri) * kH + h) * kChunkBytes,
+                             src + (h ? kUpChunk + oc : oc) * 8 * kBM, kChunkBytes, red_bar);
+              ++ri;
+            }
+          }
+        }
+      }
+    }
     if (warp >= 2) {
       const int q = warp & 3;
       const int row_in_tile = q * 32 + lane;
-      const uint32_t part_base = smem_u32(smem);
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16);  // accumulator 0
       const bool raw_int = (KIND == 2) && (p.epi.c_dtype == HX_S32) && (p.epi.epi == HX_EPI_NONE);
-      int owned = 0;
-      for (int t = t_first; t < p.total_tiles; t += t_step) {  // one tile per cluster
+      bool landed = (n_own == 0 || !via_smem) || (lane == 0 ? mbar_wait(red_bar, 0, p.timeout, abort_flag) : true);
+      landed = __shfl_sync(0xffffffffu, landed, 0);
+      if (!landed && lane == 0) {
+        raise_abort(abort_flag, p.err_flag, 5);
+        int ignored = 0;  // let copies still in flight land before the CTA exits
+        if (warp == 2) mbar_wait(red_bar, 0, p.timeout, &ignored);
+      }
+      for (int t = t_first; landed && t < p.total_tiles; t += t_step) {  // one tile per cluster
         int m_blk, n_blk;
         tile_coords(t, p, m_blk, n_blk);
         const int m = m_blk * kBM + row_in_tile;
 #pragma unroll 1
-        for (int oc = static_cast<int>(rank); oc < Cfg::kBNOut / 32; oc += S, ++owned) {
-          if ((owned & 1) != (warp - 2) / 4) continue;  // two warps per row quarter
+        for (int j = (warp - 2) / 4; j < n_own; j += 2) {  // two warps per row quarter
+          const int oc = static_cast<int>(rank) + j * S;
+          uint32_t own[32], ownu[32];
+          tmem_ld_32x32b_x32(t_row + oc * 32, own);
+          if constexpr (SWIGLU) tmem_ld_32x32b_x32(t_row + (kUpChunk + oc) * 32, ownu);
+          tmem_ld_wait();
           uint32_t r[32];
           float v[32], up[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            r[j] = 0u;
-            v[j] = 0.f;
-            up[j] = 0.f;
+          for (int jj = 0; jj < 32; ++jj) {
+            r[jj] = 0u;
+            v[jj] = 0.f;
+            up[jj] = 0.f;
           }
-          const uint32_t row_off = static_cast<uint32_t>(row_in_tile * (BN + 4) * 4);
+          int ri = 0;
+#pragma unroll 1
           for (int rr = 0; rr < S; ++rr) {
-            const uint32_t base = gemm_peer_addr(part_base + row_off, rr);
             uint32_t x[32], u[32];
+            if (rr == static_cast<int>(rank)) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)  // eight independent 16-byte DSMEM loads
-              ld_cluster_v4(base + (oc * 32 + j) * 4, x[j], x[j + 1], x[j + 2], x[j + 3]);
-            if constexpr (SWIGLU) {
+              for (int jj = 0; jj < 32; ++jj) {
+                x[jj] = own[jj];
+                u[jj] = SWIGLU ? ownu[jj] : 0u;
+              }
+            } else if (!via_smem) {  // partials too large for the ring: read them from L2
+              const uint4 *src = p.ws + (static_cast<size_t>(t) * S + rr) * (BN / 32) * 8 * kBM + row_in_tile;
 #pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                ld_cluster_v4(base + (BN / 2 + oc * 32 + j) * 4, u[j], u[j + 1], u[j + 2], u[j + 3]);
+              for (int g = 0; g < 8; ++g) {
+                const uint4 w = __ldcg(src + (oc * 8 + g) * kBM);
+                x[4 * g] = w.x;
+                x[4 * g + 1] = w.y;
+                x[4 * g + 2] = w.z;
+                x[4 * g + 3] = w.w;
+              }
+              if constexpr (SWIGLU) {
+#pragma unroll
+                for (int g = 0; g < 8; ++g) {
+                  const uint4 w = __ldcg(src + ((kUpChunk + oc) * 8 + g) * kBM);
+                  u[4 * g] = w.x;
+                  u[4 * g + 1] = w.y;
+                  u[4 * g + 2] = w.z;
+                  u[4 * g + 3] = w.w;
+                }
+              }
+            } else {
+              const uint8_t *slot = smem + ((j * (S - 1) + ri) * kH) * kChunkBytes + row_in_tile * 16;
+#pragma unroll
+              for (int g = 0; g < 8; ++g) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(slot + g * kBM * 16);
+                x[4 * g] = w.x;
+                x[4 * g + 1] = w.y;
+                x[4 * g + 2] = w.z;
+                x[4 * g + 3] = w.w;
+              }
+              if constexpr (SWIGLU) {
+#pragma unroll
+                for (int g = 0; g < 8; ++g) {
+                  const uint4 w = *reinterpret_cast<const uint4 *>(slot + kChunkBytes + g * kBM * 16);
+                  u[4 * g] = w.x;
+                  u[4 * g + 1] = w.y;
+                  u[4 * g + 2] = w.z;
+                  u[4 * g + 3] = w.w;
+                }
+              }
+              ++ri;
             }
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if constexpr (KIND == 2) r[j] += x[j];
-              else v[j] += __uint_as_float(x[j]);
-              if constexpr (SWIGLU) up[j] += __uint_as_float(u[j]);
+            for (int jj = 0; jj < 32; ++jj) {
+              if constexpr (KIND == 2) r[jj] += x[jj];
+              else v[jj] += __uint_as_float(x[jj]);
+              if constexpr (SWIGLU) up[jj] += __uint_as_float(u[jj]);
             }
           }
           if constexpr (KIND == 2) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = static_cast<float>(static_cast<int32_t>(r[j]));
+            for (int jj = 0; jj < 32; ++jj) v[jj] = static_cast<float>(static_cast<int32_t>(r[jj]));
           }
           const int n0 = n_blk * Cfg::kBNOut + oc * 32;
           if (!raw_int) epi_transform32(p.epi, v, up, m, n0);
@@ -624,8 +701,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (threadIdx.x == 64) HX_GEMM_STAMP(14);
-    gemm_cluster_sync();  // peers keep their smem until every CTA has read it
-    if (threadIdx.x == 64) HX_GEMM_STAMP(15);
+    // the reduction read this CTA's own partial from TMEM: free it only after
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
   }
 
   if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);

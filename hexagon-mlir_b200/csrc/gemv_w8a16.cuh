@@ -149,14 +149,6 @@ __global__ void __launch_bounds__(128) hx_gemv_w8a16_scalar_kernel(const GemvPar
 
 // 1-D bulk copy global -> shared completing on an mbarrier (16-byte aligned
 // addresses, size a multiple of 16).
-__device__ __forceinline__ void bulk_load_1d(void *smem_dst, const void *gsrc, uint32_t bytes,
-                                             uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
 
 struct GemvStreamParams {
   GemvParams g;

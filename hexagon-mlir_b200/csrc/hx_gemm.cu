@@ -18,6 +18,7 @@
 #include <mutex>
 #include <string>
 #include <utility>
+#include <vector>
 
 #include "gemm_chain.cuh"
 #include "launch.cuh"
@@ -157,6 +158,56 @@ __host__ __device__ inline bool aligned16(const void *p) { return (reinterpret_c
 // ------------------------------------------------------------ launch
 // launch_pdl and the tile-GEMM launchers live in launch.cuh; the kernels are
 // instantiated per input kind in gemm_kind{0,1,2}.cu (compiled in parallel).
+// ------------------------------------------------------------ split-K workspace
+// Split-K partials travel through L2 in a device buffer the library owns, one
+// per (device, stream) so concurrent streams never share one.  It grows on
+// demand outside stream capture; during capture a call that would need a
+// larger buffer runs unsplit instead.
+struct SplitWorkspace {
+  int dev;
+  cudaStream_t stream;
+  void *ptr;
+  size_t bytes;
+};
+std::mutex g_ws_mu;
+std::vector<SplitWorkspace> g_ws;
+
+int split_workspace(size_t need, cudaStream_t s, uint4 **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(g_ws_mu);
+  SplitWorkspace *w = nullptr;
+  for (auto &x : g_ws)
+    if (x.dev == dev && x.stream == s) w = &x;
+  if (w && w->bytes >= need) {
+    *out = static_cast<uint4 *>(w->ptr);
+    return HX_OK;
+  }
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(s, &st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+  if (st != cudaStreamCaptureStatusNone) return kNeedsNoSplit;
+  const size_t bytes = std::max<size_t>(need, size_t(16) << 20);
+  void *p = nullptr;
+  e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return kNeedsNoSplit;
+  }
+  if (w) {
+    // cudaFree waits for work still using the old buffer
+    e = cudaFree(w->ptr);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFree(split workspace)");
+    w->ptr = p;
+    w->bytes = bytes;
+  } else {
+    g_ws.push_back({dev, s, p, bytes});
+  }
+  *out = static_cast<uint4 *>(p);
+  return HX_OK;
+}
+
 int stage_bytes(int bn) { return kBM * kKBytes + bn * kKBytes; }
 
 // Tile plan: width BN (and, only when the caller asks, a split-K factor S).
@@ -164,7 +215,8 @@ int stage_bytes(int bn) { return kBM * kKBytes + bn * kKBytes; }
 // launch costs ~7 us of fixed latency (prologue, first loads, epilogue,
 // drain), after which each CTA streams its tiles' K blocks at ~100 GB/s of
 // TMA ingest (or the tensor rate, if slower); persistent CTAs overlap the
-// fixed part across waves.  Split-K adds ~3.5 us of DSMEM reduction.
+// fixed part across waves.  Split-K adds ~3.5 us for the exchange of fp32
+// partials through L2 and the reduction.
 inline bool best_cost_found(double c) { return c < 1e299; }
 
 void plan_tiles(int64_t M, int64_t N, int64_t K, int ez, bool swiglu, bool bmn, int sms, int &bn,
@@ -181,7 +233,9 @@ void plan_tiles(int64_t M, int64_t N, int64_t K, int ez, bool swiglu, bool bmn, 
     const int out_w = swiglu ? b / 2 : b;
     const int64_t tiles = m_tiles * ((N + out_w - 1) / out_w);
     for (int sp : {1, 2, 3, 4, 6, 8}) {
-      if (split_req == 0 ? sp != 1 : sp != split_req) continue;  // auto: no split
+      // auto plans do not split: inside the benchmark's CUDA graphs the
+      // measured gains of split plans did not hold up (split_k is explicit)
+      if (split_req == 0 ? sp != 1 : sp != split_req) continue;
       if (sp > 1 && (bmn || tiles * sp > sms || sp > k_blocks)) continue;
       const int64_t waves = (tiles * sp + sms - 1) / sms;
       const double kb = static_cast<double>((k_blocks + sp - 1) / sp);
@@ -423,6 +477,18 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
   if (splits > 1 && (total * splits > sms || splits > p.stage_blocks)) {
     if (d->split_k > 1) return unsupported("split_k: tiles x split_k exceeds the SMs or the K blocks");
     splits = p.splits = 1;
+  }
+  p.ws = nullptr;
+  p.red_smem = 0;
+  if (splits > 1) {
+    const size_t need = static_cast<size_t>(total) * splits * bn * kBM * 4;
+    rc = split_workspace(need, s, &p.ws);
+    if (rc == kNeedsNoSplit) {
+      if (d->split_k > 1) return unsupported("split_k: no workspace (stream capture or device memory)");
+      splits = p.splits = 1;
+    } else if (rc != HX_OK) {
+      return rc;
+    }
   }
   int ctas = sms;
   if (d->max_ctas > 0) ctas = std::min(ctas, static_cast<int>(d->max_ctas));

@@ -14,7 +14,10 @@ int launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
   using Cfg = GemmCfg<BN, KIND, BMN, SW>;
   auto kern = hx_gemm_sm100_kernel<BN, KIND, BMN, SW>;
   const int ring = p.stages * p.kbs * Cfg::kStageBytes;
-  const int smem = std::max(ring, p.splits > 1 ? Cfg::kPartBytes : 0) + 1024 + kBarBytes + kStageOutBytes;
+  const int fixed = 1024 + kBarBytes + kStageOutBytes;
+  GemmParams q = p;
+  q.red_smem = (p.splits > 1 && Cfg::red_bytes(p.splits) + fixed <= kMaxDynSmem) ? 1 : 0;
+  const int smem = std::max(ring, q.red_smem ? Cfg::red_bytes(p.splits) : 0) + fixed;
   if (smem > kMaxDynSmem) return unsupported("shared memory for this tile plan exceeds 227 KB");
   static std::atomic<int> configured{0};
   if (configured.load(std::memory_order_acquire) < smem) {
@@ -39,7 +42,8 @@ int launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    // Split-K needs every cluster resident at once (one tile per cluster).
+    // Split-K runs one tile per cluster; clusters that do not all fit at once
+    // would run as a second wave, so such plans fall back to no split.
     static std::atomic<int> max_clusters[9];
     int mc = max_clusters[p.splits].load(std::memory_order_acquire);
     if (mc == 0) {
@@ -49,9 +53,9 @@ int launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
     }
     if (grid / p.splits > mc) return kNeedsNoSplit;
     cfg.numAttrs = 2;
-    e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+    e = cudaLaunchKernelEx(&cfg, kern, ta, tb, q);
   } else {
-    e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, ta, tb, p);
+    e = launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, ta, tb, q);
   }
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "hx_gemm_sm100_kernel launch");
