@@ -377,6 +377,8 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
     from qcom_hexagon_backend import ops
 
     M, K, N = WL.LMHEAD_M, WL.LMHEAD_K, WL.LMHEAD_N
+    if args.lm_rows:
+        M = args.lm_rows
     ns = (N + world - 1) // world
     n0, n1 = rank * ns, min(N, (rank + 1) * ns)
     g = torch.Generator().manual_seed(1238)
@@ -410,7 +412,7 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
     line = {"metric": "GEMM+epilogue TFLOP/s", "value": round(tflops, 2), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "LM head 16384x2048x50304 bf16, column-sharded (BASELINE config 5)",
+            "config": {"workload": f"LM head {M}x2048x50304 bf16, column-sharded (BASELINE config 5)",
                        "parallelism": f"tp{world} (N-sharded, output left vocab-parallel)",
                        "l2": "inputs (1.9 GB/step) larger than L2"},
             "gpu_launches": args.steps,
@@ -456,6 +458,8 @@ def main(argv=None):
     ap.add_argument("--workload", choices=["gpt2", "qwen", "tinyllama", "lmhead"], default="gpt2")
     ap.add_argument("--batch", type=int, default=1, help="decode batch M for --workload tinyllama")
     ap.add_argument("--layers", type=int, default=22, help="decoder layers for --workload tinyllama")
+    ap.add_argument("--lm-rows", type=int, default=0,
+                    help="rows M of the LM-head GEMM (default: the config's 16384; smaller for profiling)")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU work for the CPU baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
