@@ -26,6 +26,7 @@
 
 #include "gemv_w8a16.cuh"
 #include "ptx.cuh"
+#include "w8a16_sm100.cuh"
 
 namespace hx {
 
@@ -64,6 +65,18 @@ __device__ __forceinline__ int group_find(const GroupParams &p, int item) {
     else hi = mid - 1;
   }
   return lo;
+}
+
+// c + a.lo * b.lo + a.hi * b.hi for fp16 pairs a, b, accumulated in fp32
+// (fma.rn.f32.f16: the fp16 product is exact in fp32, one rounding per step).
+__device__ __forceinline__ float fma2_f16_f32(uint32_t a2, uint32_t b2, float c) {
+  float d;
+  asm("{\n\t.reg .f16 al, ah, bl, bh;\n\t.reg .f32 t;\n\t"
+      "mov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+      "fma.rn.f32.f16 t, al, bl, %3;\n\tfma.rn.f32.f16 %0, ah, bh, t;\n\t}"
+      : "=f"(d)
+      : "r"(a2), "r"(b2), "f"(c));
+  return d;
 }
 
 __device__ __forceinline__ int ld_acquire_gpu(const int32_t *p) {
@@ -215,33 +228,30 @@ __global__ void __launch_bounds__(kGroupThreads + 32, 2)
         // four weights (one 32-bit word per row) at a time keeps MC x 4 x-values live
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          float xf[MC][4];
+          uint2 xh[MC];  // four fp16 x values of batch row m
 #pragma unroll
           for (int m = 0; m < MC; ++m) {
-            uint2 xr = make_uint2(0, 0);
+            xh[m] = make_uint2(0, 0);
             // shared memory, or L2-coherent global loads (x may have been
             // written earlier in this launch)
             if (m < p.M) {
               const uint2 *xp = reinterpret_cast<const uint2 *>(xs + m * ldxs + kv * 16 + q * 4);
-              xr = d.x_in_slot ? *xp : __ldcg(xp);
+              xh[m] = d.x_in_slot ? *xp : __ldcg(xp);
             }
-            const __half2 h0 = *reinterpret_cast<const __half2 *>(&xr.x);
-            const __half2 h1 = *reinterpret_cast<const __half2 *>(&xr.y);
-            xf[m][0] = __low2float(h0);
-            xf[m][1] = __high2float(h0);
-            xf[m][2] = __low2float(h1);
-            xf[m][3] = __high2float(h1);
           }
 #pragma unroll
           for (int r = 0; r < RMAX; ++r) {
             if (r >= rpw) break;
             const uint32_t word = q == 0 ? wv[r].x : (q == 1 ? wv[r].y : (q == 2 ? wv[r].z : wv[r].w));
-            float f[4];
-            i8x4_to_f32(word, f);
+            // exact int8 -> fp16 pairs (weights 0,1 and 2,3), then fp16 x fp16
+            // products (exact in fp32) accumulated in fp32: the same numbers as
+            // fmaf on the converted floats, in half the instructions
+            const uint32_t u = word ^ 0x80808080u;
+            const uint32_t w01 = i8x2_to_f16x2(u, 0x5150u);
+            const uint32_t w23 = i8x2_to_f16x2(u, 0x5352u);
 #pragma unroll
             for (int m = 0; m < MC; ++m)
-#pragma unroll
-              for (int e = 0; e < 4; ++e) acc[r][m] = fmaf(f[e], xf[m][e], acc[r][m]);
+              acc[r][m] = fma2_f16_f32(w23, xh[m].y, fma2_f16_f32(w01, xh[m].x, acc[r][m]));
           }
         }
       }

@@ -25,6 +25,7 @@
 #include "gemm_simt.cuh"
 #include "gemm_sm100.cuh"
 #include "gemv_grouped.cuh"
+#include "gemv_grouped_tc.cuh"
 #include "gemv_w8a16.cuh"
 #include "w8a16_sm100.cuh"
 #include "hx_gemm.h"
@@ -789,12 +790,72 @@ int gemm_chain_impl(const hx_gemm_desc *descs, const int32_t *a_dep, const int32
 }
 
 // ------------------------------------------------------------ grouped W8A16
+// Tensor-core grouped launch (gemv_grouped_tc.cuh) when every projection
+// fits it: M <= 16, at most kGtMaxProj projections, K % 128 == 0, 16-byte
+// aligned rows.  Returns kNeedsNoSplit (internal) when it does not apply.
+int gemv_grouped_tc_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32_t *counters,
+                         int32_t *error_flag, cudaStream_t s, int sms) {
+  if (M > kGtMpad || count > kGtMaxProj) return kNeedsNoSplit;
+  if (const char *env = std::getenv("HX_GROUPED_CUDA_CORE"))
+    if (std::atoi(env) > 0) return kNeedsNoSplit;
+  for (int g = 0; g < count; ++g) {
+    const hx_w8a16_proj &q = projs[g];
+    if (q.K % 128 || q.ldw % 16 || q.ldx % 8 || !aligned16(q.x) || !aligned16(q.W)) return kNeedsNoSplit;
+  }
+  static GtParams p;  // ~30 KB: built on the host, passed by value at launch
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  p.G = count;
+  p.M = static_cast<int32_t>(M);
+  p.counters = counters;
+  p.err_flag = error_flag;
+  p.timeout = kDefaultTimeout;
+  int64_t items = 0;
+  for (int g = 0; g < count; ++g) {
+    const hx_w8a16_proj &q = projs[g];
+    int rc = make_tmap3(&p.tmW[g], q.W, HX_S8, 128, static_cast<uint64_t>(q.N),
+                        static_cast<uint64_t>(q.K / 128), static_cast<uint64_t>(q.ldw), 128, kGtKbStage);
+    if (rc != HX_OK) return rc;
+    GtDesc &d = p.d[g];
+    d.x = static_cast<const __half *>(q.x);
+    d.scale = static_cast<const __half *>(q.scale);
+    d.bias = static_cast<const __half *>(q.bias);
+    d.y = static_cast<__half *>(q.y);
+    d.N = static_cast<int32_t>(q.N);
+    d.K = static_cast<int32_t>(q.K);
+    d.ldx = static_cast<int32_t>(q.ldx);
+    d.ldy = static_cast<int32_t>(q.ldy);
+    d.dep = q.dep;
+    d.item_begin = static_cast<int32_t>(items);
+    d.kblocks = static_cast<int32_t>(q.K / 128);
+    d.signal = 0;
+    if (q.dep >= 0) p.d[q.dep].signal = 1;
+    items += (q.N + 127) / 128;
+    if (items > INT32_MAX) return unsupported("too many items");
+  }
+  p.total_items = static_cast<int32_t>(items);
+  cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int32_t) * count, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(counters)");
+  static std::atomic<int> configured{0};
+  if (!configured.load(std::memory_order_acquire)) {
+    e = cudaFuncSetAttribute(hx_gemv_w8a16_grouped_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kGtSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(grouped tc)");
+    configured.store(1, std::memory_order_release);
+  }
+  const int grid = static_cast<int>(std::min<int64_t>(items, sms));
+  e = launch_pdl(hx_gemv_w8a16_grouped_tc_kernel, dim3(grid), dim3(kGtThreads), kGtSmemBytes, s, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "hx_gemv_w8a16_grouped_tc_kernel");
+  return HX_OK;
+}
+
 int gemv_grouped_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32_t *counters,
                       int32_t *error_flag, cudaStream_t s) {
   if (M < 0 || count < 0) return arg_fail("negative size");
   if (count == 0 || M == 0) return HX_OK;
   if (count > kGroupMax) return unsupported("more projections than one grouped launch takes (256)");
-  if (M > 8) return unsupported("grouped W8A16 takes M <= 8");
+  if (M > kGtMpad) return unsupported("grouped W8A16 takes M <= 16");
   if (!projs || !counters) return arg_fail("null projections or counters");
   int sms = 0, major = 0;
   int rc = current_device_info(&sms, &major);
@@ -803,6 +864,17 @@ int gemv_grouped_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32_t 
     g_last_error = "current device is not sm_100";
     return HX_E_NO_DEVICE;
   }
+  for (int g = 0; g < count; ++g) {  // validate before choosing a kernel
+    const hx_w8a16_proj &q = projs[g];
+    if (q.N <= 0 || q.K <= 0 || !q.x || !q.W || !q.scale || !q.y) return arg_fail("bad projection");
+    if (q.ldx < q.K || q.ldw < q.K || q.ldy < q.N) return arg_fail("leading dimension too small");
+    if (q.N > INT32_MAX || q.K > INT32_MAX || q.ldx > INT32_MAX || q.ldw > INT32_MAX || q.ldy > INT32_MAX)
+      return unsupported("size");
+    if (q.dep >= g || q.dep < -1) return arg_fail("dep must name an earlier projection or be -1");
+  }
+  rc = gemv_grouped_tc_impl(M, count, projs, counters, error_flag, s, sms);
+  if (rc != kNeedsNoSplit) return rc;
+  if (M > 8) return unsupported("grouped W8A16 on CUDA cores takes M <= 8");
   static GroupParams p;  // 18 KB: built on the host, passed by value at launch
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);

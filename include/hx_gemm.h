@@ -186,9 +186,12 @@ typedef struct hx_w8a16_proj {
 } hx_w8a16_proj;
 
 /* Run up to 256 W8A16 projections (a decode step's linears) in one
-   persistent launch, M <= 8, K % 16 == 0, 16-byte aligned rows.  Weight rows
+   persistent launch, M <= 16, K % 16 == 0, 16-byte aligned rows.  Weight rows
    stream into shared memory ahead of use; dependent projections wait on
-   per-projection completion counters.  `counters` is caller-owned device
+   per-projection completion counters.  Lists of at most 156 projections whose
+   K are all multiples of 128 run on the tensor cores (int8 -> fp16 exact
+   conversion, tcgen05 UMMA, fp32 accumulation); other lists, which must then
+   have M <= 8, run on CUDA cores.  `counters` is caller-owned device
    scratch of `count` int32, zeroed by this call (cudaMemsetAsync on the
    stream).  Same per-projection arithmetic as hx_gemv_w8a16 (reference:
    dequantise + matmul, LinalgToLLVMPass.cpp:203-209); the grouping itself

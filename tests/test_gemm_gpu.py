@@ -358,10 +358,22 @@ def test_cpu_tensor_rejected(cuda_device):
 
 
 # ---------------------------------------------------------------- grouped W8A16
-@pytest.mark.parametrize("M", [1, 3, 8])
-def test_w8a16_grouped_chain(cuda_device, M):
+GROUPED_TC_SHAPES = [(2048, 2048, -1, 0.0015), (256, 2048, -1, 0.02), (5632, 2048, -1, 0.0015),
+                     (2048, 2048, 0, 0.02), (2048, 5632, 2, 0.02), (300, 1024, -1, 0.02)]
+GROUPED_MIXED_SHAPES = GROUPED_TC_SHAPES[:5] + [(100, 48, -1, 0.02)]  # K=48: CUDA-core kernel
+
+
+@pytest.mark.parametrize("path,M", [("tc", 1), ("tc", 3), ("tc", 8), ("tc", 16),
+                                    ("mixed", 1), ("mixed", 3), ("mixed", 8),
+                                    ("cuda_core", 1), ("cuda_core", 8)])
+def test_w8a16_grouped_chain(cuda_device, monkeypatch, path, M):
     """A decode-layer-like list in one launch: independent projections plus a
-    dependent chain (q -> o, gate -> down), checked against the oracle."""
+    dependent chain (q -> o, gate -> down), checked against the oracle.
+    "tc": every K a multiple of 128, the tensor-core kernel; "mixed": one
+    K=48 projection sends the list to the CUDA-core kernel; "cuda_core":
+    the CUDA-core kernel forced through HX_GROUPED_CUDA_CORE."""
+    if path == "cuda_core":
+        monkeypatch.setenv("HX_GROUPED_CUDA_CORE", "1")
     q = hx()
     d = cuda_device
     g = torch.Generator().manual_seed(30 + M)
@@ -372,8 +384,7 @@ def test_w8a16_grouped_chain(cuda_device, M):
         return w, s
 
     x = torch.randn(M, 2048, generator=g).half()
-    shapes = [(2048, 2048, -1, 0.0015), (256, 2048, -1, 0.02), (5632, 2048, -1, 0.0015),
-              (2048, 2048, 0, 0.02), (2048, 5632, 2, 0.02), (100, 48, -1, 0.02)]
+    shapes = GROUPED_MIXED_SHAPES if path == "mixed" else GROUPED_TC_SHAPES
     grp = q.ops.W8A16Group(M, d)
     ys, ws = [], []
     for i, (n, k, dep, shi) in enumerate(shapes):
