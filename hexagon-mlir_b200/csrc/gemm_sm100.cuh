@@ -73,6 +73,7 @@ struct GemmParams {
   int32_t *err_flag;              // optional global error word
   uint4 *ws;                      // split-K: [tile][rank][BN/32][8][128] x 16 B of partials
   int32_t red_smem;               // split-K: fetch remote partials into the ring (else read L2)
+  int32_t b_const;                // B is constant: fetch the first B tiles before the dependency wait
   EpiArgs epi;
 };
 
@@ -334,12 +335,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // Prologue done: let the next kernel in the stream start its own, then
-  // wait for the previous one before reading or writing global memory.
+  // Prologue done: let the next kernel in the stream start its own.  The
+  // producer and the epilogue wait for the previous one before touching
+  // global memory (griddepcontrol.wait below); the UMMA warp touches none.
   grid_dep_launch_dependents();
   if (threadIdx.x == 0) HX_GEMM_STAMP(1);
-  grid_dep_wait();
-  if (threadIdx.x == 0) HX_GEMM_STAMP(2);
 
   // Split-K: the CTAs of a cluster share each tile; CTA `rank` streams stage
   // blocks [sb_begin, sb_end) of it.  Without split-K: the whole K range.
@@ -352,59 +352,83 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    auto load_a = [&](uint64_t *fb, int stage, int m0, int sb) {
+      uint8_t *dstA = sA + stage * A_ST;
+      if (!B_MN && p.use3d)
+        tma_load_3d(dstA, &tmA, fb, 0, m0, sb * p.kbs);
+      else
+        tma_load_2d(dstA, &tmA, fb, sb * Cfg::kBKElems, m0);
+    };
+    auto load_b = [&](uint64_t *fb, int stage, int n_blk, int sb) {
+      uint8_t *dstB = sB + stage * B_ST;
+      if constexpr (B_MN) {  // kbs == 1, 2-D maps
+        const int kx = sb * Cfg::kBKElems;
+        const int n0 = n_blk * BN;
+#pragma unroll
+        for (int j = 0; j < BN / Cfg::kMNChunk; ++j)
+          tma_load_2d(dstB + j * (Cfg::kBKElems * 128), &tmB, fb, n0 + j * Cfg::kMNChunk, kx);
+      } else if (p.use3d) {
+        const int kz = sb * p.kbs;
+        if constexpr (SWIGLU) {
+          const int n0 = n_blk * (BN / 2);
+          tma_load_3d(dstB, &tmB, fb, 0, n0, kz);
+          tma_load_3d(dstB + B_ST / 2, &tmB, fb, 0, p.n_half + n0, kz);
+        } else {
+          tma_load_3d(dstB, &tmB, fb, 0, n_blk * BN, kz);
+        }
+      } else {  // kbs == 1, 2-D maps
+        const int kx = sb * Cfg::kBKElems;
+        if constexpr (SWIGLU) {
+          const int n0 = n_blk * (BN / 2);
+          tma_load_2d(dstB, &tmB, fb, kx, n0);
+          tma_load_2d(dstB + B_ST / 2, &tmB, fb, kx, p.n_half + n0);
+        } else {
+          tma_load_2d(dstB, &tmB, fb, kx, n_blk * BN);
+        }
+      }
+    };
+    // Constant B (model weights): the first tile's first stages of B are
+    // fetched before waiting for the previous kernel, overlapping its tail.
+    int pre = 0;
+    if (p.b_const && t_first < p.total_tiles) pre = min(STAGES, sb_end - sb_begin);
+    if (lane == 0 && pre > 0) {
+      int m_blk, n_blk;
+      tile_coords(t_first, p, m_blk, n_blk);
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full_bar[i], A_ST + B_ST);
+        load_b(&full_bar[i], i, n_blk, sb_begin + i);
+      }
+    }
+    grid_dep_wait();
+    if (threadIdx.x == 0) HX_GEMM_STAMP(2);
     int stage = 0;
     uint32_t phase = 0;
-    int64_t issued = 0;
+    int64_t issued = pre;
     bool ok = true;
     for (int t = t_first; t < p.total_tiles && ok; t += t_step) {
       int m_blk, n_blk;
       tile_coords(t, p, m_blk, n_blk);
       const int m0 = m_blk * kBM;
       for (int sb = sb_begin; sb < sb_end; ++sb) {
-        bool w = (lane == 0) ? mbar_wait(&empty_bar[stage], phase ^ 1, p.timeout, abort_flag)
-                             : true;
-        w = __shfl_sync(0xffffffffu, w, 0);
-        if (!w) {
-          if (lane == 0) raise_abort(abort_flag, p.err_flag, 1);
-          ok = false;
-          break;
+        const bool early = (t == t_first) && (sb - sb_begin < pre);  // B already in flight
+        if (!early) {
+          bool w = (lane == 0) ? mbar_wait(&empty_bar[stage], phase ^ 1, p.timeout, abort_flag)
+                               : true;
+          w = __shfl_sync(0xffffffffu, w, 0);
+          if (!w) {
+            if (lane == 0) raise_abort(abort_flag, p.err_flag, 1);
+            ok = false;
+            break;
+          }
         }
         if (lane == 0) {
           uint64_t *fb = &full_bar[stage];
-          mbar_arrive_expect_tx(fb, A_ST + B_ST);
-          uint8_t *dstA = sA + stage * A_ST;
-          uint8_t *dstB = sB + stage * B_ST;
-          if constexpr (B_MN) {  // kbs == 1, 2-D maps
-            const int kx = sb * Cfg::kBKElems;
-            tma_load_2d(dstA, &tmA, fb, kx, m0);
-            const int n0 = n_blk * BN;
-#pragma unroll
-            for (int j = 0; j < BN / Cfg::kMNChunk; ++j)
-              tma_load_2d(dstB + j * (Cfg::kBKElems * 128), &tmB, fb, n0 + j * Cfg::kMNChunk, kx);
-          } else if (p.use3d) {
-            const int kz = sb * p.kbs;
-            tma_load_3d(dstA, &tmA, fb, 0, m0, kz);
-            if constexpr (SWIGLU) {
-              const int n0 = n_blk * (BN / 2);
-              tma_load_3d(dstB, &tmB, fb, 0, n0, kz);
-              tma_load_3d(dstB + B_ST / 2, &tmB, fb, 0, p.n_half + n0, kz);
-            } else {
-              tma_load_3d(dstB, &tmB, fb, 0, n_blk * BN, kz);
-            }
-          } else {  // kbs == 1, 2-D maps
-            const int kx = sb * Cfg::kBKElems;
-            tma_load_2d(dstA, &tmA, fb, kx, m0);
-            if constexpr (SWIGLU) {
-              const int n0 = n_blk * (BN / 2);
-              tma_load_2d(dstB, &tmB, fb, kx, n0);
-              tma_load_2d(dstB + B_ST / 2, &tmB, fb, kx, p.n_half + n0);
-            } else {
-              tma_load_2d(dstB, &tmB, fb, kx, n_blk * BN);
-            }
-          }
+          if (!early) mbar_arrive_expect_tx(fb, A_ST + B_ST);
+          load_a(fb, stage, m0, sb);
+          if (!early) load_b(fb, stage, n_blk, sb);
         }
         __syncwarp();
-        ++issued;
+        if (!early) ++issued;
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1;
@@ -506,6 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    grid_dep_wait();  // C / residual / bias may come from the previous kernel
     const int q = warp & 3;                   // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
     int it = 0;

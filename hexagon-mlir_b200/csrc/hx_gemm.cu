@@ -225,8 +225,9 @@ void plan_tiles(int64_t M, int64_t N, int64_t K, int ez, bool swiglu, bool bmn, 
   const int64_t m_tiles = (M + kBM - 1) / kBM;
   const int64_t k_blocks = (K * ez + kKBytes - 1) / kKBytes;
   const double flop_per_us_sm = 10.9e6 * (ez == 1 ? 2.0 : 1.0);
-  double best = 1e300;
-  int best_bn = bn ? bn : 128, best_s = 1;
+  // best plan without split-K, and best with it
+  double best1 = 1e300, bestS = 1e300;
+  int bn1 = bn ? bn : 128, bnS = bn1, sS = 1;
   for (int b : {256, 192, 128, 96, 64}) {
     if (bn && b != bn) continue;
     if (bmn && ez == 1 && b < 128) continue;
@@ -234,24 +235,40 @@ void plan_tiles(int64_t M, int64_t N, int64_t K, int ez, bool swiglu, bool bmn, 
     const int out_w = swiglu ? b / 2 : b;
     const int64_t tiles = m_tiles * ((N + out_w - 1) / out_w);
     for (int sp : {1, 2, 3, 4, 6, 8}) {
-      // auto plans do not split: inside the benchmark's CUDA graphs the
-      // measured gains of split plans did not hold up (split_k is explicit)
-      if (split_req == 0 ? sp != 1 : sp != split_req) continue;
+      // auto: 1, 2 or 4 CTAs per cluster (clusters of 3, 6 and 8 pack poorly)
+      if (split_req == 0 ? (sp == 3 || sp > 4) : sp != split_req) continue;
       if (sp > 1 && (bmn || tiles * sp > sms || sp > k_blocks)) continue;
       const int64_t waves = (tiles * sp + sms - 1) / sms;
       const double kb = static_cast<double>((k_blocks + sp - 1) / sp);
       const double ingest = kb * stage_bytes(b) / 100e3;
       const double mma = kb * (2.0 * kBM * b * (kKBytes / ez)) / flop_per_us_sm;
       const double cost = 7.0 + waves * std::max(ingest, mma) + (sp > 1 ? 3.5 : 0.0);
+      double &best = sp > 1 ? bestS : best1;
       if (cost < best * 0.97) {  // prefer the earlier (wider) option on near ties
         best = cost;
-        best_bn = b;
-        best_s = sp;
+        if (sp > 1) {
+          bnS = b;
+          sS = sp;
+        } else {
+          bn1 = b;
+        }
       }
     }
   }
-  bn = best_bn;
-  splits = best_cost_found(best) ? best_s : (split_req > 1 ? split_req : 1);
+  // Auto plans split only for a large predicted gain: measured inside CUDA
+  // graphs, smaller predicted gains did not hold up.
+  const bool take_split = best_cost_found(bestS) &&
+                          (split_req > 1 || !best_cost_found(best1) || bestS < 0.85 * best1);
+  if (take_split) {
+    bn = bnS;
+    splits = sS;
+  } else if (best_cost_found(best1)) {
+    bn = bn1;
+    splits = 1;
+  } else {  // no feasible plan: let the caller's checks report why
+    bn = bn1;
+    splits = split_req > 1 ? split_req : 1;
+  }
 }
 
 int validate(const hx_gemm_desc *d) {
@@ -274,6 +291,7 @@ int validate(const hx_gemm_desc *d) {
     default: return unsupported("C dtype");
   }
   if (d->b_layout != HX_B_NK && d->b_layout != HX_B_KN) return arg_fail("b_layout");
+  if (d->flags & ~HX_GEMM_B_CONST) return arg_fail("unknown flags bits");
   if (d->M == 0 || d->N == 0) return HX_OK;
   if (!d->C || (d->K > 0 && (!d->A || !d->B))) return arg_fail("null A/B/C");
   if (d->lda < std::max<int64_t>(d->K, 1)) return arg_fail("lda < K");
@@ -481,6 +499,7 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
   }
   p.ws = nullptr;
   p.red_smem = 0;
+  p.b_const = (d->flags & HX_GEMM_B_CONST) ? 1 : 0;
   if (splits > 1) {
     const size_t need = static_cast<size_t>(total) * splits * bn * kBM * 4;
     rc = split_workspace(need, s, &p.ws);

@@ -33,6 +33,7 @@ HX_F16, HX_BF16, HX_S8, HX_S32, HX_F32 = 0, 1, 2, 3, 4
 # B layouts
 HX_B_NK, HX_B_KN = 0, 1
 # hx_gemv_w8a16_ex flags
+HX_GEMM_B_CONST = 1
 HX_GEMV_WEIGHTS_CONST = 1
 HX_GEMV_FORCE_CUDA_CORE = 2
 # epilogues
@@ -88,7 +89,7 @@ class HxGemmDesc(ctypes.Structure):
         ("error_flag", ctypes.c_void_p),
         ("timeout_cycles", ctypes.c_uint64),
         ("split_k", ctypes.c_int32),
-        ("reserved0", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
     ]
 
 

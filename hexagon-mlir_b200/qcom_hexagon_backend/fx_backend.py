@@ -41,20 +41,23 @@ _ADD_FNS = (operator.add, torch.add, operator.iadd)
 _MUL_FNS = (operator.mul, torch.mul)
 
 
-def hx_linear(x, weight, bias=None, residual=None, activation=None):
-    """Fused linear used as the call_function target of rewritten nodes."""
+def hx_linear(x, weight, bias=None, residual=None, activation=None, weight_const=False):
+    """Fused linear used as the call_function target of rewritten nodes.
+    weight_const: the weight is a module parameter/buffer (constant while the
+    compiled forward runs), so the kernel may prefetch it early."""
     if residual is not None:
         out_shape = (*x.shape[:-1], weight.shape[0])
         if tuple(residual.shape) != out_shape or residual.dtype != x.dtype:
             # Broadcasting residual: not an epilogue the kernel fuses.
-            y = ops.linear(x, weight, bias, activation=activation)
+            y = ops.linear(x, weight, bias, activation=activation, b_const=weight_const)
             ops.chain_flush()  # the add below reads y
             return y + residual
-    return ops.linear(x, weight, bias, activation=activation, residual=residual)
+    return ops.linear(x, weight, bias, activation=activation, residual=residual, b_const=weight_const)
 
 
 def hx_swiglu(x, weight_gate_up):
-    return ops.linear(x, weight_gate_up, None, activation="swiglu")
+    # the fused [gate; up] weight is a buffer the rewrite registered: constant
+    return ops.linear(x, weight_gate_up, None, activation="swiglu", b_const=True)
 
 
 def _users(n: fx.Node):
@@ -168,6 +171,8 @@ def rewrite(gm: fx.GraphModule) -> fx.GraphModule:
             w = _src(graph, s.weight)
             b = _src(graph, s.bias)
             kwargs = {}
+            if s.weight[0] == "attr":
+                kwargs["weight_const"] = True
             if act:
                 kwargs["activation"] = act
             if residual is not None:

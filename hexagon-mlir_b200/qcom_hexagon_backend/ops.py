@@ -78,17 +78,20 @@ def gemm(
     error_flag: Optional[torch.Tensor] = None,
     timeout_cycles: int = 0,
     split_k: int = 0,
+    b_const: bool = False,
 ) -> torch.Tensor:
     """out = epilogue(a @ B) with B = b.T (b_layout "nk", b is W[N,K]) or
     B = b (b_layout "kn", b is [K,N]).
 
     For epilogue "swiglu", b is the fused [gate; up] weight of 2N rows and
-    out = silu(a @ gate.T) * (a @ up.T) has N columns.
+    out = silu(a @ gate.T) * (a @ up.T) has N columns.  b_const: b is a
+    constant (model weights) nothing earlier in the stream writes, so the
+    kernel may start fetching it before the previous kernel ends.
     """
     d, out, dev = make_desc(a, b, b_layout=b_layout, out=out, out_dtype=out_dtype, epilogue=epilogue,
                             bias=bias, residual=residual, scale=scale, tile_n=tile_n, stages=stages,
                             max_ctas=max_ctas, force_simt=force_simt, error_flag=error_flag,
-                            timeout_cycles=timeout_cycles, split_k=split_k)
+                            timeout_cycles=timeout_cycles, split_k=split_k, b_const=b_const)
     rec = _recorder
     if rec is not None and rec.device == dev:
         if rec.accepts(d, a, b, residual, b_layout, tile_n, stages, max_ctas, force_simt):
@@ -212,7 +215,7 @@ def chain_flush(*args):
 
 def make_desc(a, b, *, b_layout="nk", out=None, out_dtype=None, epilogue="none", bias=None,
               residual=None, scale=None, tile_n=0, stages=0, max_ctas=0, force_simt=False,
-              error_flag=None, timeout_cycles=0, split_k=0):
+              error_flag=None, timeout_cycles=0, split_k=0, b_const=False):
     """Validate the tensors and fill an hx_gemm_desc; returns (desc, out, device).
     The tensors must stay alive while the descriptor is in use."""
     _check_cuda(a, "a")
@@ -283,6 +286,7 @@ def make_desc(a, b, *, b_layout="nk", out=None, out_dtype=None, epilogue="none",
         d.error_flag = error_flag.data_ptr()
     d.timeout_cycles = timeout_cycles
     d.split_k = split_k
+    d.flags = _lib.HX_GEMM_B_CONST if b_const else 0
     return d, out, dev
 
 

@@ -106,10 +106,17 @@ typedef struct hx_gemm_desc {
                               whose bounded wait ran out                      */
   uint64_t timeout_cycles; /* bound for each device wait (0 = ~2 s default)   */
   int32_t split_k;         /* CTAs (2..8, one thread-block cluster) sharing a
-                              tile's K range, partials reduced through
-                              distributed shared memory; 1 = off, 0 = auto   */
-  int32_t reserved0;
+                              tile's K range, fp32 partials exchanged through
+                              an L2 workspace the library owns; 1 = off,
+                              0 = automatic                                   */
+  int32_t flags;           /* HX_GEMM_* bits below                            */
 } hx_gemm_desc;
+
+/* B holds constants (model weights) that no work still running before this
+   call in the stream writes: the kernel may fetch its first B tiles before
+   waiting for that work (programmatic dependent launch), overlapping the
+   previous kernel's tail.  Use only when that holds. */
+#define HX_GEMM_B_CONST 1
 
 /* C = epilogue(A . B).  Replaces the linalg.matmul + linalg.generic pair the
    reference compiles through LinalgToLLVMPass

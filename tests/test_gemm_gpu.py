@@ -473,3 +473,37 @@ def test_pair_int8_exact(cuda_device, force_pairs):
 def test_pair_default_for_large_gemm(cuda_device):
     """A GEMM with a full wave of 256x256 tiles takes the pair kernel by default."""
     run_and_check(4096, 4096, 1024, torch.bfloat16, "none", seed=53)
+
+
+# ---------------------------------------------------------------- constant-B prefetch
+@pytest.mark.parametrize("tile_n", [64, 128, 192, 256])
+def test_b_const_back_to_back(cuda_device, tile_n):
+    """HX_GEMM_B_CONST: the weights of a GEMM are fetched before the previous
+    kernel in the stream ends; its A (the previous GEMM's output) must still
+    be read only after that kernel completes."""
+    q = hx()
+    g = torch.Generator().manual_seed(60 + tile_n)
+    x = torch.randn(512, 768, generator=g).half()
+    w1 = (torch.randn(1024, 768, generator=g) * 0.02).half()
+    w2 = (torch.randn(768, 1024, generator=g) * 0.02).half()
+    b1 = torch.randn(1024, generator=g).half()
+    xd, w1d, w2d, b1d = x.cuda(), w1.cuda(), w2.cuda(), b1.cuda()
+    for _ in range(3):
+        y1 = q.gemm(xd, w1d, epilogue="bias_gelu_tanh", bias=b1d, b_const=True, tile_n=tile_n)
+        y2 = q.gemm(y1, w2d, epilogue="residual", residual=xd, b_const=True)
+    torch.cuda.synchronize()
+    r1 = O.linear_ref(to_np32(x), to_np32(w1), epilogue="bias_gelu_tanh", bias=to_np32(b1))
+    assert_close(to_np32(y1), r1)
+    r2 = O.linear_ref(to_np32(y1), to_np32(w2), epilogue="residual", residual=to_np32(x))
+    assert_close(to_np32(y2), r2)
+
+
+def test_unknown_flags_rejected(cuda_device):
+    import ctypes
+    from qcom_hexagon_backend import _lib
+    q = hx()
+    a = torch.randn(64, 64, device="cuda").half()
+    d, out, dev = q.ops.make_desc(a, torch.randn(64, 64, device="cuda").half())
+    d.flags = 0x40
+    rc = _lib.load().hx_gemm(ctypes.byref(d), None)
+    assert rc == _lib.HX_E_INVALID_ARG
