@@ -9,14 +9,15 @@
 // caps that kernel near 40% of HBM bandwidth; here the weights only pass
 // through an exact int8 -> fp16 conversion and the products run on the tensor
 // cores with the operands swapped (as in w8a16_sm100.cuh):
-//   D^T[n, m] = W[n, :] . x[m, :]   (UMMA M = 128 weight rows, N = 16 >= M)
+//   D^T[n, m] = W[n, :] . x[m, :]   (UMMA M = 128 weight rows, N = M padded
+//                                    to 16, 32 or 64)
 //
 // Work item = (projection g, block of 128 weight rows); CTA c of the
 // persistent grid (one per SM) takes items c, c + grid, ...  Roles (448 threads):
 //   warp 0      producer: one 3-D TMA load per 4 K blocks (128 rows x 512 B =
 //               64 KB of int8) into a 2-stage ring; never waits on
 //               dependencies, so the weight stream runs ahead of the math
-//   warp 1      TMEM allocator + UMMA issuer (2 x 16-column accumulators)
+//   warp 1      TMEM allocator + UMMA issuer (2 accumulators of N columns)
 //   warps 2..9  converters (two per row quarter, half a row each):
 //               int8 (TMA 128B-swizzled) -> fp16 A tile, and the x rows of the
 //               K block -> fp16 B tile (rows >= M zero), both 128B-swizzled
@@ -44,17 +45,26 @@ namespace hx {
 constexpr int kGtMaxProj = 156;                          // projections per launch (param space)
 constexpr int kGtConvWarps = 8;
 constexpr int kGtThreads = (2 + kGtConvWarps + 4) * 32;
-constexpr int kGtMpad = 16;                              // UMMA N: batch rows, padded
+constexpr int kGtMaxM = 64;                              // largest batch (UMMA N <= 64)
 constexpr int kGtKbStage = 4;                            // 128-byte K blocks per W stage
 constexpr int kGtWStages = 2;
 constexpr int kGtCStages = 2;
 constexpr int kGtWStageBytes = kGtKbStage * 128 * 128;   // 64 KB of int8 W
 constexpr int kGtABytes = 2 * 128 * 128;                 // fp16 W, 128 rows x 128 K
-constexpr int kGtXBytes = 2 * kGtMpad * 128;             // fp16 x, 16 rows x 128 K
-constexpr int kGtCStageBytes = kGtABytes + kGtXBytes;    // 36 KB
-constexpr int kGtSmemBytes = kGtWStages * kGtWStageBytes + kGtCStages * kGtCStageBytes + 1024 + 256;
 constexpr int kGtEpiWarps = 4;
-constexpr uint32_t kGtIdesc = make_idesc(0, false, 128, kGtMpad);
+
+// MPAD: the batch M padded to the UMMA N (16, 32 or 64).
+template <int MPAD>
+struct GtCfg {
+  static constexpr int kXBytes = 2 * MPAD * 128;                  // fp16 x, MPAD rows x 128 K
+  static constexpr int kCStageBytes = kGtABytes + kXBytes;        // 36 / 40 / 48 KB
+  static constexpr int kSmemBytes = kGtWStages * kGtWStageBytes + kGtCStages * kCStageBytes + 1024 + 256;
+  static constexpr uint32_t kIdesc = make_idesc(0, false, 128, MPAD);
+  static constexpr int kTmemCols = 2 * MPAD < 32 ? 32 : 2 * MPAD;  // two accumulators
+  static constexpr int kXPieces = MPAD * 16 / 256;                // 16-byte x pieces per converter thread
+  static_assert(MPAD == 16 || MPAD == 32 || MPAD == 64, "MPAD");
+  static_assert(kSmemBytes <= 232448, "shared memory");
+};
 
 struct GtDesc {
   const __half *x;
@@ -107,14 +117,16 @@ __device__ __forceinline__ void gt_fail(volatile int *abort_flag, int32_t *err, 
   if (err) atomicExch(err, code);
 }
 
+template <int MPAD>
 __global__ void __launch_bounds__(kGtThreads, 1)
     hx_gemv_w8a16_grouped_tc_kernel(const __grid_constant__ GtParams p) {
+  using Cfg = GtCfg<MPAD>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t *wring = smem;
   uint8_t *cring = smem + kGtWStages * kGtWStageBytes;
-  uint64_t *wfull = reinterpret_cast<uint64_t *>(cring + kGtCStages * kGtCStageBytes);
+  uint64_t *wfull = reinterpret_cast<uint64_t *>(cring + kGtCStages * Cfg::kCStageBytes);
   uint64_t *wempty = wfull + kGtWStages;   // converters finished a W stage (8 arrivals)
   uint64_t *cfull = wempty + kGtWStages;   // converted A + x ready (8 arrivals)
   uint64_t *cempty = cfull + kGtCStages;   // UMMAs finished reading (commit)
@@ -143,7 +155,7 @@ __global__ void __launch_bounds__(kGtThreads, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 32);
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -222,14 +234,14 @@ __global__ void __launch_bounds__(kGtThreads, 1)
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t a_base = smem_u32(cring + cs * kGtCStageBytes);
+          const uint32_t a_base = smem_u32(cring + cs * Cfg::kCStageBytes);
           const uint32_t b_base = a_base + kGtABytes;
 #pragma unroll
           for (int h = 0; h < 2; ++h)
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              umma_f16(tmem_base + acc * kGtMpad, sdesc_kmajor_sw128(a_base + h * (128 * 128) + k * 32),
-                       sdesc_kmajor_sw128(b_base + h * (kGtMpad * 128) + k * 32), kGtIdesc,
+              umma_f16(tmem_base + acc * MPAD, sdesc_kmajor_sw128(a_base + h * (128 * 128) + k * 32),
+                       sdesc_kmajor_sw128(b_base + h * (MPAD * 128) + k * 32), Cfg::kIdesc,
                        (kb > 0 || h > 0 || k > 0) ? 1u : 0u);
           umma_commit(&cempty[cs]);
           any = true;
@@ -255,7 +267,6 @@ __global__ void __launch_bounds__(kGtThreads, 1)
     const int r = (cw & 3) * 32 + lane;     // weight row this thread converts
     const int c_lo = (cw >> 2) * kCPT;      // its chunks of the row: c_lo .. c_lo+kCPT-1
     const int tid = cw * 32 + lane;         // < 256: one 16-byte piece of the K block's x tile
-    const int xm = tid >> 4, xh = (tid >> 3) & 1, xc = tid & 7;
     int ws = 0, cs = 0;
     uint32_t wph = 0, cph = 0;
     bool ok = true;
@@ -284,7 +295,6 @@ __global__ void __launch_bounds__(kGtThreads, 1)
           break;
         }
       }
-      const __half *xrow = d.x + static_cast<int64_t>(xm) * d.ldx + xh * 64 + xc * 8;
       for (int kb0 = 0; kb0 < d.kblocks && ok; kb0 += kGtKbStage) {
         bool w = (lane == 0) ? GT_WAIT(3, mbar_wait(&wfull[ws], wph, p.timeout, abort_flag)) : true;
         w = __shfl_sync(0xffffffffu, w, 0);
@@ -297,10 +307,17 @@ __global__ void __launch_bounds__(kGtThreads, 1)
         for (int j = 0; j < nk; ++j) {
           // this thread's x piece: through L1 when x predates the launch, else
           // coherent from L2; its latency overlaps the slot wait and conversion
-          uint4 xv = make_uint4(0u, 0u, 0u, 0u);
-          if (tid < 256 && xm < p.M) {
-            const uint4 *xp = reinterpret_cast<const uint4 *>(xrow + (kb0 + j) * 128);
-            xv = d.dep < 0 ? __ldg(xp) : __ldcg(xp);
+          uint4 xv[Cfg::kXPieces];
+#pragma unroll
+          for (int i = 0; i < Cfg::kXPieces; ++i) {
+            const int pc = tid + i * 256;
+            const int xm = pc >> 4, xh = (pc >> 3) & 1, xc = pc & 7;
+            xv[i] = make_uint4(0u, 0u, 0u, 0u);
+            if (xm < p.M) {
+              const uint4 *xp = reinterpret_cast<const uint4 *>(
+                  d.x + static_cast<int64_t>(xm) * d.ldx + (kb0 + j) * 128 + xh * 64 + xc * 8);
+              xv[i] = d.dep < 0 ? __ldg(xp) : __ldcg(xp);
+            }
           }
           w = (lane == 0) ? GT_WAIT(4, mbar_wait(&cempty[cs], cph ^ 1, p.timeout, abort_flag)) : true;
           w = __shfl_sync(0xffffffffu, w, 0);
@@ -309,7 +326,7 @@ __global__ void __launch_bounds__(kGtThreads, 1)
             ok = false;
             break;
           }
-          uint8_t *cst = cring + cs * kGtCStageBytes;
+          uint8_t *cst = cring + cs * Cfg::kCStageBytes;
           // weight row r, chunks c_lo.. : int8 (TMA 128B-swizzled) -> fp16 in the
           // 64-K half c_lo / 4
           const uint8_t *raw = wring + ws * kGtWStageBytes + j * (128 * 128) + r * 128;
@@ -324,10 +341,14 @@ __global__ void __launch_bounds__(kGtThreads, 1)
             *reinterpret_cast<uint4 *>(dst + ((j0 ^ (r & 7)) << 4)) = lo;
             *reinterpret_cast<uint4 *>(dst + (((j0 + 1) ^ (r & 7)) << 4)) = hi;
           }
-          // x rows of this K block (fp16, 16 rows x 2 halves x 8 chunks; rows >= M zero)
-          if (tid < 256)
-            *reinterpret_cast<uint4 *>(cst + kGtABytes + xh * (kGtMpad * 128) + xm * 128 +
-                                     ((xc ^ (xm & 7)) << 4)) = xv;
+          // x rows of this K block (fp16, MPAD rows x 2 halves x 8 chunks; rows >= M zero)
+#pragma unroll
+          for (int i = 0; i < Cfg::kXPieces; ++i) {
+            const int pc = tid + i * 256;
+            const int xm = pc >> 4, xh = (pc >> 3) & 1, xc = pc & 7;
+            *reinterpret_cast<uint4 *>(cst + kGtABytes + xh * (MPAD * 128) + xm * 128 +
+                                       ((xc ^ (xm & 7)) << 4)) = xv[i];
+          }
           fence_proxy_async_smem();  // generic smem writes -> visible to the UMMAs
           __syncwarp();
           if (lane == 0) mbar_arrive(&cfull[cs]);
@@ -361,20 +382,25 @@ __global__ void __launch_bounds__(kGtThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t v[16];
-      tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kGtMpad, v);
-      tmem_ld_wait();
+      const int n = (item - d.item_begin) * 128 + q * 32 + lane;
+      const float sc = n < d.N ? __half2float(d.scale[n]) : 0.f;
+      const float b = (n < d.N && d.bias) ? __half2float(d.bias[n]) : 0.f;
+#pragma unroll
+      for (int c = 0; c < MPAD / 16; ++c) {
+        if (c * 16 >= p.M) break;
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * MPAD + c * 16, v);
+        tmem_ld_wait();
+        if (n < d.N) {
+#pragma unroll
+          for (int m = 0; m < 16; ++m)
+            if (c * 16 + m < p.M)
+              d.y[static_cast<int64_t>(c * 16 + m) * d.ldy + n] = __float2half_rn(__uint_as_float(v[m]) * sc + b);
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);  // the accumulator may be reused
-      const int n = (item - d.item_begin) * 128 + q * 32 + lane;
-      if (n < d.N) {
-        const float sc = __half2float(d.scale[n]);
-        const float b = d.bias ? __half2float(d.bias[n]) : 0.f;
-#pragma unroll
-        for (int m = 0; m < kGtMpad; ++m)
-          if (m < p.M) d.y[static_cast<int64_t>(m) * d.ldy + n] = __float2half_rn(__uint_as_float(v[m]) * sc + b);
-      }
       if (d.signal) {  // this warp's y stores, then one count
         __syncwarp();
         if (lane == 0) {
@@ -391,7 +417,7 @@ __global__ void __launch_bounds__(kGtThreads, 1)
 #ifdef HX_GT_PROF
   if (threadIdx.x == 0) atomicAdd(&g_gt_prof[blockIdx.x][6], (unsigned long long)(clock64() - gt_start_));
 #endif
-  if (warp == 1) tmem_dealloc(tmem_base, 32);
+  if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
 }
 
 }  // namespace hx

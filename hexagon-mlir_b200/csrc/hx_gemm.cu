@@ -810,11 +810,11 @@ int gemm_chain_impl(const hx_gemm_desc *descs, const int32_t *a_dep, const int32
 
 // ------------------------------------------------------------ grouped W8A16
 // Tensor-core grouped launch (gemv_grouped_tc.cuh) when every projection
-// fits it: M <= 16, at most kGtMaxProj projections, K % 128 == 0, 16-byte
+// fits it: M <= 64, at most kGtMaxProj projections, K % 128 == 0, 16-byte
 // aligned rows.  Returns kNeedsNoSplit (internal) when it does not apply.
 int gemv_grouped_tc_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32_t *counters,
                          int32_t *error_flag, cudaStream_t s, int sms) {
-  if (M > kGtMpad || count > kGtMaxProj) return kNeedsNoSplit;
+  if (M > kGtMaxM || count > kGtMaxProj) return kNeedsNoSplit;
   if (const char *env = std::getenv("HX_GROUPED_CUDA_CORE"))
     if (std::atoi(env) > 0) return kNeedsNoSplit;
   for (int g = 0; g < count; ++g) {
@@ -855,15 +855,19 @@ int gemv_grouped_tc_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32
   p.total_items = static_cast<int32_t>(items);
   cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int32_t) * count, s);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(counters)");
-  static std::atomic<int> configured{0};
-  if (!configured.load(std::memory_order_acquire)) {
-    e = cudaFuncSetAttribute(hx_gemv_w8a16_grouped_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kGtSmemBytes);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(grouped tc)");
-    configured.store(1, std::memory_order_release);
-  }
   const int grid = static_cast<int>(std::min<int64_t>(items, sms));
-  e = launch_pdl(hx_gemv_w8a16_grouped_tc_kernel, dim3(grid), dim3(kGtThreads), kGtSmemBytes, s, p);
+  auto launch = [&](auto kern, int smem, std::atomic<int> &configured) -> cudaError_t {
+    if (!configured.load(std::memory_order_acquire)) {
+      cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (r != cudaSuccess) return r;
+      configured.store(1, std::memory_order_release);
+    }
+    return launch_pdl(kern, dim3(grid), dim3(kGtThreads), smem, s, p);
+  };
+  static std::atomic<int> conf16{0}, conf32{0}, conf64{0};
+  if (M <= 16) e = launch(hx_gemv_w8a16_grouped_tc_kernel<16>, GtCfg<16>::kSmemBytes, conf16);
+  else if (M <= 32) e = launch(hx_gemv_w8a16_grouped_tc_kernel<32>, GtCfg<32>::kSmemBytes, conf32);
+  else e = launch(hx_gemv_w8a16_grouped_tc_kernel<64>, GtCfg<64>::kSmemBytes, conf64);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "hx_gemv_w8a16_grouped_tc_kernel");
   return HX_OK;
@@ -874,7 +878,7 @@ int gemv_grouped_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32_t 
   if (M < 0 || count < 0) return arg_fail("negative size");
   if (count == 0 || M == 0) return HX_OK;
   if (count > kGroupMax) return unsupported("more projections than one grouped launch takes (256)");
-  if (M > kGtMpad) return unsupported("grouped W8A16 takes M <= 16");
+  if (M > kGtMaxM) return unsupported("grouped W8A16 takes M <= 64");
   if (!projs || !counters) return arg_fail("null projections or counters");
   int sms = 0, major = 0;
   int rc = current_device_info(&sms, &major);

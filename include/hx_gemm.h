@@ -193,7 +193,7 @@ typedef struct hx_w8a16_proj {
 } hx_w8a16_proj;
 
 /* Run up to 256 W8A16 projections (a decode step's linears) in one
-   persistent launch, M <= 16, K % 16 == 0, 16-byte aligned rows.  Weight rows
+   persistent launch, M <= 64, K % 16 == 0, 16-byte aligned rows.  Weight rows
    stream into shared memory ahead of use; dependent projections wait on
    per-projection completion counters.  Lists of at most 156 projections whose
    K are all multiples of 128 run on the tensor cores (int8 -> fp16 exact

@@ -363,7 +363,8 @@ GROUPED_TC_SHAPES = [(2048, 2048, -1, 0.0015), (256, 2048, -1, 0.02), (5632, 204
 GROUPED_MIXED_SHAPES = GROUPED_TC_SHAPES[:5] + [(100, 48, -1, 0.02)]  # K=48: CUDA-core kernel
 
 
-@pytest.mark.parametrize("path,M", [("tc", 1), ("tc", 3), ("tc", 8), ("tc", 16),
+@pytest.mark.parametrize("path,M", [("tc", 1), ("tc", 3), ("tc", 8), ("tc", 16), ("tc", 17),
+                                    ("tc", 32), ("tc", 50), ("tc", 64),
                                     ("mixed", 1), ("mixed", 3), ("mixed", 8),
                                     ("cuda_core", 1), ("cuda_core", 8)])
 def test_w8a16_grouped_chain(cuda_device, monkeypatch, path, M):
