@@ -127,6 +127,9 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- dist
+CHAIN = False  # --chain
+
+
 def dist_setup(n_gpus):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -178,7 +181,7 @@ def build_gpt2(dev, seed=1234):
     x = torch.randn(1024, 768, generator=g).half()
     launcher = TorchMLIRHexagonLauncher()
     cg = launcher.compile_torch_mlir(model, [x], "gpt2_linear_stack",
-                                     HexagonOptions(device=dev.index))
+                                     HexagonOptions(device=dev.index, chain_gemms=CHAIN))
     flops = WL.gpt2_stack_flops()
     return dict(launcher=launcher, model=model, cg=cg, x=x, flops=flops, launches=cg.n_hx_calls,
                 metric="GEMM+epilogue TFLOP/s", unit="TFLOP/s", dtype="fp16",
@@ -195,7 +198,8 @@ def build_qwen(dev, seed=1235):
     g = torch.Generator().manual_seed(seed)
     x = torch.randn(2048, 896, generator=g).to(torch.bfloat16)
     launcher = TorchMLIRHexagonLauncher()
-    cg = launcher.compile_torch_mlir(model, [x], "qwen_linear_stack", HexagonOptions(device=dev.index))
+    cg = launcher.compile_torch_mlir(model, [x], "qwen_linear_stack",
+                                     HexagonOptions(device=dev.index, chain_gemms=CHAIN))
     flops = WL.qwen_stack_flops()
     return dict(launcher=launcher, model=model, cg=cg, x=x, flops=flops, launches=cg.n_hx_calls,
                 metric="GEMM+epilogue TFLOP/s", unit="TFLOP/s", dtype="bf16",
@@ -504,6 +508,8 @@ def main(argv=None):
     ap.add_argument("--workload", choices=["gpt2", "qwen", "tinyllama", "lmhead"], default="gpt2")
     ap.add_argument("--batch", type=int, default=1, help="decode batch M for --workload tinyllama")
     ap.add_argument("--layers", type=int, default=22, help="decoder layers for --workload tinyllama")
+    ap.add_argument("--chain", action="store_true",
+                    help="stacks: run consecutive linears as one persistent launch (chain_gemms)")
     ap.add_argument("--lm-dtype", choices=["bf16", "int8"], default="bf16",
                     help="LM head: bf16, or the int8 W8A8 variant (int32 accumulate)")
     ap.add_argument("--lm-rows", type=int, default=0,
@@ -511,6 +517,8 @@ def main(argv=None):
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU work for the CPU baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
+    global CHAIN
+    CHAIN = args.chain
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":
