@@ -74,7 +74,7 @@ class HexagonOptions:
     enableVTCMTiling: bool = True
     enableHVXInlining: bool = False
     enableSeedLayoutConversions: bool = False
-    tileSizes: str = ""  # B200: "N" or "N,stages" tile override (N in 64/128/256)
+    tileSizes: str = ""  # B200: "N" or "N,stages" tile override (N in 64/96/128/192/256)
     lowerConstantsInSeparateSharedObjects: bool = False
     enableLWP: bool = False
     disableLWPLoop: bool = False
@@ -110,8 +110,8 @@ class HexagonOptions:
             vals = [int(p) for p in parts]
         except ValueError:
             raise ValueError(f"tileSizes must be 'N' or 'N,stages', got {self.tileSizes!r}") from None
-        if not vals or len(vals) > 2 or vals[0] not in (64, 128, 256):
-            raise ValueError(f"tileSizes must be 'N' or 'N,stages' with N in 64/128/256, got {self.tileSizes!r}")
+        if not vals or len(vals) > 2 or vals[0] not in (64, 96, 128, 192, 256):
+            raise ValueError(f"tileSizes must be 'N' or 'N,stages' with N in 64/96/128/192/256, got {self.tileSizes!r}")
         stages = vals[1] if len(vals) == 2 else 0
         if stages and not 2 <= stages <= 8:
             raise ValueError("stages must be in [2, 8]")
