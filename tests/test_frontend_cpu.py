@@ -39,10 +39,11 @@ def test_options_validation_and_override():
     with pytest.raises(ValueError):
         HexagonOptions(target_artifact="exe")
     with pytest.raises(ValueError):
-        HexagonOptions(tileSizes="96")
+        HexagonOptions(tileSizes="100")
     with pytest.raises(ValueError):
         HexagonOptions(tileSizes="128,9")
     assert HexagonOptions(tileSizes="256, 4").tile_override() == (256, 4)
+    assert HexagonOptions(tileSizes="192").tile_override() == (192, 0)
     assert HexagonOptions().tile_override() == (0, 0)
     o = HexagonOptions.from_dict(HexagonOptions().__dict__)
     assert o.hash() == HexagonOptions().hash()
