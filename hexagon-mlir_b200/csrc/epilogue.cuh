@@ -35,6 +35,8 @@ struct EpiArgs {
   int32_t r_vec_ok;    // residual rows are 16-byte aligned
   int32_t b_vec_ok;    // bias is 16-byte aligned
   int32_t s_vec_ok;    // scale is 16-byte aligned
+  int32_t n_peers;     // > 0: every stored chunk also goes to peer_C[0..n_peers)
+  void *peer_C[7];     //   (other GPUs' buffers, same offsets and ldc as C)
   int32_t pre16;       // every operand the epilogue reads (scale, bias,
                        // residual) is 16-bit and 16-byte aligned: full
                        // 32-column chunks may be prefetched raw (Pre16)
@@ -355,16 +357,18 @@ __device__ __forceinline__ void epi_store32(const EpiArgs &e, const float (&v)[3
           pk[j] = *reinterpret_cast<uint32_t *>(&h);
         }
       }
-      uint16_t *cp = static_cast<uint16_t *>(e.C) + base;
-      if (full && e.c_vec_ok) {
-        uint4 *dst = reinterpret_cast<uint4 *>(cp);
+      for (int tgt = -1; tgt < e.n_peers; ++tgt) {  // C, then the peers' copies
+        uint16_t *cp = static_cast<uint16_t *>(tgt < 0 ? e.C : e.peer_C[tgt]) + base;
+        if (full && e.c_vec_ok) {
+          uint4 *dst = reinterpret_cast<uint4 *>(cp);
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-      } else {
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (n0 + j < e.N) cp[j] = static_cast<uint16_t>(pk[j >> 1] >> ((j & 1) * 16));
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < e.N) cp[j] = static_cast<uint16_t>(pk[j >> 1] >> ((j & 1) * 16));
+        }
       }
       break;
     }
@@ -378,16 +382,18 @@ __device__ __forceinline__ void epi_store32(const EpiArgs &e, const float (&v)[3
         else
           w[j] = raw_int ? raw[j] : static_cast<uint32_t>(__float2int_rn(v[j]));
       }
-      uint32_t *cp = static_cast<uint32_t *>(e.C) + base;
-      if (full && e.c_vec_ok) {
-        uint4 *dst = reinterpret_cast<uint4 *>(cp);
+      for (int tgt = -1; tgt < e.n_peers; ++tgt) {  // C, then the peers' copies
+        uint32_t *cp = static_cast<uint32_t *>(tgt < 0 ? e.C : e.peer_C[tgt]) + base;
+        if (full && e.c_vec_ok) {
+          uint4 *dst = reinterpret_cast<uint4 *>(cp);
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
-          dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-      } else {
+          for (int q = 0; q < 8; ++q)
+            dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+        } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (n0 + j < e.N) cp[j] = w[j];
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < e.N) cp[j] = w[j];
+        }
       }
       break;
     }
@@ -462,9 +468,12 @@ __device__ __forceinline__ void epi_store32_staged_t(const EpiArgs &e, const flo
     for (int i = 0; i < 4; ++i) {
       const int r = i * 8 + (lane >> 2);
       const uint4 x = *reinterpret_cast<const uint4 *>(stg + r * 64 + ((qq ^ ((r >> 1) & 3)) << 4));
-      if (m0 + r < e.M)
-        *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(e.C) + static_cast<int64_t>(m0 + r) * e.ldc +
-                                   n0 + qq * 8) = x;
+      if (m0 + r < e.M) {
+        const int64_t off = static_cast<int64_t>(m0 + r) * e.ldc + n0 + qq * 8;
+        *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(e.C) + off) = x;
+        for (int t = 0; t < e.n_peers; ++t)  // fused all-gather: the same chunk to every peer
+          *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(e.peer_C[t]) + off) = x;
+      }
     }
   } else {
     uint32_t w[32];
@@ -489,9 +498,12 @@ __device__ __forceinline__ void epi_store32_staged_t(const EpiArgs &e, const flo
     for (int i = 0; i < 8; ++i) {
       const int r = i * 4 + (lane >> 3);
       const uint4 x = *reinterpret_cast<const uint4 *>(stg + r * 128 + ((qq ^ (r & 7)) << 4));
-      if (m0 + r < e.M)
-        *reinterpret_cast<uint4 *>(static_cast<uint32_t *>(e.C) + static_cast<int64_t>(m0 + r) * e.ldc +
-                                   n0 + qq * 4) = x;
+      if (m0 + r < e.M) {
+        const int64_t off = static_cast<int64_t>(m0 + r) * e.ldc + n0 + qq * 4;
+        *reinterpret_cast<uint4 *>(static_cast<uint32_t *>(e.C) + off) = x;
+        for (int t = 0; t < e.n_peers; ++t)  // fused all-gather: the same chunk to every peer
+          *reinterpret_cast<uint4 *>(static_cast<uint32_t *>(e.peer_C[t]) + off) = x;
+      }
     }
   }
   __syncwarp();  // the next chunk may overwrite stg

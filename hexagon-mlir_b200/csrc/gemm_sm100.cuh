@@ -732,6 +732,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
   }
 
+  // fused all-gather: peer stores are visible system-wide before the grid ends
+  if (p.epi.n_peers > 0) __threadfence_system();
   if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
   if (threadIdx.x == 0) HX_GEMM_STAMP(7);
 }

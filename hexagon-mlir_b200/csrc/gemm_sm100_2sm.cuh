@@ -294,6 +294,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   gemm_cluster_sync();  // the pair finished: no more remote arrivals or UMMA writes
   tc_fence_after();
+  // fused all-gather: peer stores are visible system-wide before the grid ends
+  if (p.epi.n_peers > 0) __threadfence_system();
   if (warp == 1) tmem_dealloc_pair(tmem_base, kTmemCols);
 }
 

@@ -334,6 +334,8 @@ int validate(const hx_gemm_desc *d) {
 
 EpiArgs make_epi(const hx_gemm_desc *d) {
   EpiArgs e;
+  e.n_peers = 0;
+  for (int i = 0; i < 7; ++i) e.peer_C[i] = nullptr;
   e.C = d->C;
   e.ldc = d->ldc;
   e.bias = d->bias;
@@ -390,7 +392,13 @@ int run_simt(const hx_gemm_desc *d, cudaStream_t s) {
   return HX_OK;
 }
 
-int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
+// Other GPUs' copies of C for the fused all-gather (hx_sharded_gemm_gather_p2p).
+struct PeerTargets {
+  int n;
+  void *C[7];
+};
+
+int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = nullptr) {
   int rc = validate(d);
   if (rc != HX_OK) return rc;
   if (d->M == 0 || d->N == 0) return HX_OK;
@@ -492,6 +500,10 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s) {
   p.timeout = d->timeout_cycles ? d->timeout_cycles : kDefaultTimeout;
   p.err_flag = d->error_flag;
   p.epi = make_epi(d);
+  if (peers) {
+    p.epi.n_peers = peers->n;
+    for (int j = 0; j < peers->n; ++j) p.epi.peer_C[j] = peers->C[j];
+  }
 
   if (splits > 1 && (total * splits > sms || splits > p.stage_blocks)) {
     if (d->split_k > 1) return unsupported("split_k: tiles x split_k exceeds the SMs or the K blocks");
@@ -1036,6 +1048,56 @@ int nccl_fail(int r, const char *where) {
 }  // namespace
 
 // ============================================================ C ABI
+// ------------------------------------------------------------ fused all-gather over NVLink
+namespace hx {
+namespace {
+struct PeerBarrierArgs {
+  int32_t *flags[8];  // flags[r]: rank r's flag array (world int32), in its GPU memory
+  int32_t rank, world, value;
+  uint64_t timeout;
+  int32_t *err_flag;
+};
+
+// One warp: lane p != rank publishes `value` into peer p's slot for this rank
+// (release, system scope), then waits (acquire, bounded) until peer p has
+// published at least `value` into this rank's array.  On timeout the error
+// word is set and the kernel returns: nothing hangs.
+__global__ void peer_barrier_kernel(const __grid_constant__ PeerBarrierArgs a) {
+  const int p = threadIdx.x;
+  if (p >= a.world || p == a.rank) return;
+  int32_t *remote = a.flags[p] + a.rank;
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(remote), "r"(a.value) : "memory");
+  const int32_t *mine = a.flags[a.rank] + p;
+  const uint64_t t0 = clock64();
+  for (;;) {
+    int32_t v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+    if (v >= a.value) break;
+    if (static_cast<uint64_t>(clock64() - t0) > a.timeout) {
+      if (a.err_flag) atomicExch(a.err_flag, 41);
+      break;
+    }
+    __nanosleep(256);
+  }
+}
+
+int peer_barrier(int32_t *const *flags, int rank, int world, int32_t value, int32_t *err_flag,
+                 cudaStream_t s) {
+  PeerBarrierArgs a;
+  for (int i = 0; i < 8; ++i) a.flags[i] = i < world ? flags[i] : nullptr;
+  a.rank = rank;
+  a.world = world;
+  a.value = value;
+  a.timeout = kDefaultTimeout;
+  a.err_flag = err_flag;
+  peer_barrier_kernel<<<1, 32, 0, s>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "peer_barrier_kernel");
+  return HX_OK;
+}
+}  // namespace
+}  // namespace hx
+
 extern "C" {
 
 int hx_version(void) { return HX_VERSION; }
@@ -1205,6 +1267,89 @@ int hx_nccl_comm_destroy(void *comm) {
   int r = g_nccl.comm_destroy(comm);
   if (r != 0) return nccl_fail(r, "ncclCommDestroy");
   return HX_OK;
+}
+
+int hx_peer_alloc(int64_t bytes, void **dev_ptr, void *ipc_handle) {
+  if (bytes <= 0 || !dev_ptr || !ipc_handle) return HX_E_INVALID_ARG;
+  hx::g_last_error.clear();
+  void *p = nullptr;
+  cudaError_t e = cudaMalloc(&p, static_cast<size_t>(bytes));
+  if (e != cudaSuccess) return hx::cuda_fail(e, "cudaMalloc(peer buffer)");
+  e = cudaMemset(p, 0, static_cast<size_t>(bytes));
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t *>(ipc_handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return hx::cuda_fail(e, "cudaIpcGetMemHandle");
+  }
+  *dev_ptr = p;
+  return HX_OK;
+}
+
+int hx_peer_handle_size(void) { return static_cast<int>(sizeof(cudaIpcMemHandle_t)); }
+
+int hx_peer_open(const void *ipc_handle, void **peer_ptr) {
+  if (!ipc_handle || !peer_ptr) return HX_E_INVALID_ARG;
+  hx::g_last_error.clear();
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return hx::cuda_fail(e, "cudaIpcOpenMemHandle");
+  return HX_OK;
+}
+
+int hx_peer_close(void *peer_ptr) {
+  if (!peer_ptr) return HX_E_INVALID_ARG;
+  cudaError_t e = cudaIpcCloseMemHandle(peer_ptr);
+  if (e != cudaSuccess) return hx::cuda_fail(e, "cudaIpcCloseMemHandle");
+  return HX_OK;
+}
+
+int hx_peer_free(void *dev_ptr) {
+  if (!dev_ptr) return HX_E_INVALID_ARG;
+  cudaError_t e = cudaFree(dev_ptr);
+  if (e != cudaSuccess) return hx::cuda_fail(e, "cudaFree(peer buffer)");
+  return HX_OK;
+}
+
+int hx_sharded_gemm_gather_p2p(const hx_gemm_desc *d, int rank, int world, void *const *gathered,
+                               int32_t *const *flags, int32_t epoch, int32_t *error_flag,
+                               void *stream) {
+  hx::g_last_error.clear();
+  if (!d || !gathered || !flags || world < 1 || world > 8 || rank < 0 || rank >= world || epoch < 0 ||
+      epoch > (INT32_MAX - 2) / 2)
+    return HX_E_INVALID_ARG;
+  for (int r = 0; r < world; ++r)
+    if (!gathered[r] || !flags[r]) return HX_E_INVALID_ARG;
+  if (d->ldc != d->N) {
+    hx::g_last_error = "gather needs a contiguous shard (ldc == N)";
+    return HX_E_INVALID_ARG;
+  }
+  const int ez = hx::esize(d->a_dtype), cz = hx::esize(d->c_dtype);
+  if (d->K == 0 || d->force_simt || d->b_layout != HX_B_NK || !hx::aligned16(d->A) || !hx::aligned16(d->B) ||
+      (d->lda * ez) % 16 || (d->ldb * ez) % 16 || (d->N * cz) % 16 ||
+      reinterpret_cast<uintptr_t>(gathered[rank]) % 16) {
+    hx::g_last_error = "fused gather needs the tensor-core path: W[N,K], K > 0, 16-byte aligned rows";
+    return HX_E_UNSUPPORTED;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Entry: every peer reached this call (its earlier readers of its buffer
+  // are stream-ordered before it), so its buffer may be overwritten.
+  int rc = hx::peer_barrier(flags, rank, world, 2 * epoch + 1, error_flag, s);
+  if (rc != HX_OK) return rc;
+  // This rank's shard lands at gathered[r][rank] on every rank r.
+  const size_t off = static_cast<size_t>(rank) * d->M * d->N * cz;
+  hx_gemm_desc dd = *d;
+  dd.C = static_cast<uint8_t *>(gathered[rank]) + off;
+  dd.split_k = 1;
+  if (!dd.error_flag) dd.error_flag = error_flag;
+  hx::PeerTargets peers;
+  peers.n = 0;
+  for (int r = 0; r < world; ++r)
+    if (r != rank) peers.C[peers.n++] = static_cast<uint8_t *>(gathered[r]) + off;
+  rc = hx::gemm_impl(&dd, s, &peers);
+  if (rc != HX_OK) return rc;
+  // Exit: every peer's stores into this rank's buffer are complete.
+  return hx::peer_barrier(flags, rank, world, 2 * epoch + 2, error_flag, s);
 }
 
 int hx_sharded_gemm_allgather(const hx_gemm_desc *d, int rank, int world, void *comm,

@@ -238,6 +238,33 @@ int hx_gemv_w8a16_grouped_noalloc(int64_t M, int count,
 int hx_sharded_gemm_allgather(const hx_gemm_desc *d, int rank, int world,
                               void *comm, void *gathered, void *stream);
 
+/* Fused column-sharded GEMM + all-gather over NVLink (no NCCL): the GEMM's
+   epilogue stores every output chunk of this rank's shard both into its own
+   buffer and, with plain stores through peer pointers, into every other
+   rank's, so the gather overlaps the math tile by tile.  gathered[r] is rank
+   r's [world][M][N] buffer (N = this shard's width, ldc == N), flags[r] its
+   array of `world` int32 (both from hx_peer_alloc, opened on the other ranks
+   with hx_peer_open); this rank's shard lands at gathered[r][rank] on every r.
+   A bounded flag barrier runs before (peers may be overwritten) and after
+   (all peers' shards arrived); `epoch` must count 0, 1, 2, ... across calls
+   on one set of buffers, and every rank must make the same calls.  A barrier
+   that times out sets *error_flag (41) instead of hanging.  W[N,K] layout,
+   K > 0, 16-byte aligned rows; at most 8 ranks.  Reference: none (the
+   reference has no multi-device path; this replaces GEMM + NCCL all-gather). */
+int hx_sharded_gemm_gather_p2p(const hx_gemm_desc *d, int rank, int world, void *const *gathered,
+                               int32_t *const *flags, int32_t epoch, int32_t *error_flag,
+                               void *stream);
+
+/* Device memory other processes' GPUs can map: cudaMalloc'ed and zeroed on the
+   current device, exported as a CUDA IPC handle of hx_peer_handle_size()
+   bytes.  hx_peer_open maps a peer's handle into this process (peer access
+   over NVLink); hx_peer_close / hx_peer_free release them. */
+int hx_peer_handle_size(void);
+int hx_peer_alloc(int64_t bytes, void **dev_ptr, void *ipc_handle);
+int hx_peer_open(const void *ipc_handle, void **peer_ptr);
+int hx_peer_close(void *peer_ptr);
+int hx_peer_free(void *dev_ptr);
+
 /* dst[M, world*Ns] = concat over r of src[r][M][Ns] along columns
    (elem_bytes per element). */
 int hx_shards_to_rows(const void *src, void *dst, int world, int64_t M,
