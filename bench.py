@@ -403,7 +403,8 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
     w = w.contiguous().to(dev)
     odt = torch.int32 if int8 else torch.bfloat16
     out = torch.empty(M, ns, dtype=odt, device=dev)
-    chunks = 4 if (world > 1 and M % 4 == 0) else 1
+    p2p = world > 1 and args.gather == "p2p"
+    chunks = 4 if (world > 1 and not p2p and M % 4 == 0) else 1
     mc = M // chunks
     gathered = torch.empty(chunks, world * mc, ns, dtype=odt, device=dev) if world > 1 else None
     side = torch.cuda.Stream(dev) if world > 1 else None
@@ -413,9 +414,16 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
     def gemm_only():
         ops.gemm(a, w, out=out)
 
+    if p2p:
+        from qcom_hexagon_backend.sharding import P2PGather
+        pg = P2PGather(M, ns, odt)
+
     def step():
         if world == 1:
             return gemm_only()
+        if p2p:  # one launch: the GEMM's epilogue writes every rank's buffer over NVLink
+            pg.run(a, w)
+            return
         for c in range(chunks):
             ops.gemm(a[c * mc:(c + 1) * mc], w, out=out[c * mc:(c + 1) * mc])
             evs_c[c].record(main)
@@ -458,18 +466,24 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
             "scaling": "strong", "vs_baseline": None, "dtype": "int8" if int8 else "bf16", "data": "synthetic",
             "config": {"workload": f"LM head {M}x2048x50304 {dtname}, column-sharded (BASELINE config 5)",
                        "parallelism": f"tp{world} (N-sharded"
-                       + (", logits all-gathered over NCCL into [world, M, N/world], overlapped in "
-                          f"{chunks} M-chunks)" if world > 1 else ")"),
+                       + ((", logits all-gathered into [world, M, N/world] by the GEMM's own epilogue "
+                           "stores over NVLink (fused, hx_sharded_gemm_gather_p2p))" if p2p else
+                           ", logits all-gathered over NCCL into [world, M, N/world], overlapped in "
+                           f"{chunks} M-chunks)") if world > 1 else ")"),
                        "l2": "inputs (1.9 GB/step) larger than L2"},
             "gemm_only": {"value": round(flops / (gemm_ms / 1e3) / 1e12, 2), "unit": unit,
                           "ms_per_step": round(gemm_ms, 4)},
-            "gpu_launches": args.steps * chunks,
+            "gpu_launches": args.steps * (3 if p2p else chunks),
             "roofline": {"bound": "tensor", "achieved": round(my_tflops, 2), "peak": peak, "unit": unit,
                          "frac": round(my_tflops / peak, 4),
                          "traffic": None if int8 else read_traffic("gemm_lmhead.txt"),
                          "kernel": "hx_gemm_sm100_2sm_kernel",
                          "peak_source": f"{peak_src} {peak_key}" + (" x2 (int8 dense rate)" if int8 else "")},
             "clocks": clocks}
+    if p2p:
+        if int(pg.error_flag.item()) != 0:
+            line["error"] = f"fused gather error flag {int(pg.error_flag.item())}"
+        pg.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -510,6 +524,8 @@ def main(argv=None):
     ap.add_argument("--layers", type=int, default=22, help="decoder layers for --workload tinyllama")
     ap.add_argument("--chain", action="store_true",
                     help="stacks: run consecutive linears as one persistent launch (chain_gemms)")
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="nccl",
+                    help="LM head at N>1: fused GEMM + NVLink all-gather (p2p) or GEMM + NCCL")
     ap.add_argument("--lm-dtype", choices=["bf16", "int8"], default="bf16",
                     help="LM head: bf16, or the int8 W8A8 variant (int32 accumulate)")
     ap.add_argument("--lm-rows", type=int, default=0,

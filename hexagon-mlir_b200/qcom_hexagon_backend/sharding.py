@@ -135,3 +135,101 @@ class ColumnShardedLinear:
                                                ctypes.c_void_p(ops._stream_ptr(dev)))
         _lib.check(rc, "hx_sharded_gemm_allgather")
         return rows_from_shards(gathered, self.N)
+
+
+class P2PGather:
+    """Fused sharded GEMM + all-gather over NVLink (hx_sharded_gemm_gather_p2p).
+
+    Every rank owns a [world, M, ns] gather buffer and a flag array in its own
+    GPU memory; the buffers are exported as CUDA IPC handles, exchanged with
+    torch.distributed and mapped by every other rank.  run(x, w) computes this
+    rank's shard x @ w.T and its GEMM epilogue writes each output chunk into
+    all ranks' buffers at [rank], so when it returns (stream-ordered) the
+    buffer holds every rank's shard.  All ranks must call run() the same
+    number of times (it synchronises them on the GPU, with bounded waits).
+    """
+
+    def __init__(self, M: int, ns: int, dtype: torch.dtype, group=None):
+        lib = _lib.load()
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("the fused gather takes at most 8 ranks")
+        self.M, self.ns, self.dtype, self.group = M, ns, dtype, group
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        esz = torch.empty(0, dtype=dtype).element_size()
+        hsz = lib.hx_peer_handle_size()
+        self._mine = []
+        handles = []
+        for nbytes in (self.world * M * ns * esz, 256):  # gather buffer, flags
+            ptr, h = ctypes.c_void_p(), (ctypes.c_uint8 * hsz)()
+            _lib.check(lib.hx_peer_alloc(nbytes, ctypes.byref(ptr), h), "hx_peer_alloc")
+            self._mine.append(ptr.value)
+            handles.append(bytes(h))
+        blob = torch.tensor(list(b"".join(handles)), dtype=torch.uint8, device=self.device)
+        allb = torch.empty(self.world * blob.numel(), dtype=torch.uint8, device=self.device)
+        dist.all_gather_into_tensor(allb, blob, group=group)
+        allb = bytes(allb.cpu().numpy().tobytes())
+        self._opened = []
+        bufs, flags = [], []
+        for r in range(self.world):
+            if r == self.rank:
+                bufs.append(self._mine[0])
+                flags.append(self._mine[1])
+                continue
+            ptrs = []
+            for j in range(2):
+                off = (r * 2 + j) * hsz
+                h = (ctypes.c_uint8 * hsz).from_buffer_copy(allb[off:off + hsz])
+                p = ctypes.c_void_p()
+                _lib.check(lib.hx_peer_open(h, ctypes.byref(p)), "hx_peer_open")
+                self._opened.append(p.value)
+                ptrs.append(p.value)
+            bufs.append(ptrs[0])
+            flags.append(ptrs[1])
+        self._bufs = (ctypes.c_void_p * self.world)(*bufs)
+        self._flags = (ctypes.c_void_p * self.world)(*flags)
+        self.epoch = 0
+        self.error_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._local_view = _device_view(self._mine[0], (self.world, M, ns), dtype, self.device)
+
+    def run(self, x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Returns this rank's [world, M, ns] buffer holding all shards."""
+        d, _, dev = ops.make_desc(x, w, out=self._local_view[self.rank], bias=bias,
+                                  epilogue="bias" if bias is not None else "none", b_const=True)
+        lib = _lib.load()
+        with torch.cuda.device(dev):
+            rc = lib.hx_sharded_gemm_gather_p2p(ctypes.byref(d), self.rank, self.world, self._bufs,
+                                                self._flags, self.epoch,
+                                                ctypes.c_void_p(self.error_flag.data_ptr()),
+                                                ctypes.c_void_p(ops._stream_ptr(dev)))
+        _lib.check(rc, "hx_sharded_gemm_gather_p2p")
+        self.epoch += 1
+        return self._local_view
+
+    def close(self):
+        lib = _lib.load()
+        torch.cuda.synchronize(self.device)
+        for p in self._opened:
+            lib.hx_peer_close(ctypes.c_void_p(p))
+        self._opened = []
+        if self.group is not None or dist.is_initialized():
+            dist.barrier(group=self.group)  # peers unmapped before the memory goes
+        for p in self._mine:
+            lib.hx_peer_free(ctypes.c_void_p(p))
+        self._mine = []
+
+
+def _device_view(ptr: int, shape, dtype, device) -> torch.Tensor:
+    """A tensor over device memory the library allocated (no copy, not owned)."""
+    class _Holder:
+        pass
+
+    h = _Holder()
+    numel = 1
+    for s in shape:
+        numel *= s
+    esz = torch.empty(0, dtype=dtype).element_size()
+    h.__cuda_array_interface__ = {"shape": (numel,), "typestr": {1: "|u1", 2: "<u2", 4: "<u4"}[esz],
+                                  "data": (ptr, False), "version": 3, "strides": None}
+    flat = torch.as_tensor(h, device=device)
+    return flat.view(dtype).view(*shape)

@@ -1,7 +1,9 @@
 """Multi-GPU parity of the column-sharded GEMM (BASELINE config 5 shape,
 scaled down): every rank computes its column shard with hx kernels and the
-full logits are assembled (a) with torch.distributed NCCL all-gather and (b)
-with the library's own NCCL communicator (hx_sharded_gemm_allgather).
+full logits are assembled (a) with torch.distributed NCCL all-gather, (b)
+with the library's own NCCL communicator (hx_sharded_gemm_allgather) and (c)
+by the fused GEMM whose epilogue stores into every rank's buffer over NVLink
+(hx_sharded_gemm_gather_p2p).
 Needs >= 2 GPUs; runs as child processes, one per GPU."""
 
 import os
@@ -42,8 +44,18 @@ WORKER = textwrap.dedent(r'''
     e3 = O.max_rel_err(local[:, : n1 - n0], ref[:, n0:n1])
     assert y1.shape == (M, N) and y2.shape == (M, N), (y1.shape, y2.shape)
     assert e1 <= 1e-2 and e2 <= 1e-2 and e3 <= 1e-2, (e1, e2, e3)
+    # (c) the fused GEMM + NVLink all-gather: several calls in a row
+    pg = S.P2PGather(M, lin.ns, torch.bfloat16)
+    for it in range(3):
+        buf = pg.run(a.cuda() * (it + 1), lin.weight)
+        torch.cuda.synchronize()
+        assert int(pg.error_flag.item()) == 0, int(pg.error_flag.item())
+        y4 = S.rows_from_shards(buf, N).float().cpu().numpy()
+        e4 = O.max_rel_err(y4, ref * (it + 1))
+        assert y4.shape == (M, N) and e4 <= 1e-2, (it, e4)
+    pg.close()
     torch.cuda.synchronize(); comm.close(); dist.destroy_process_group()
-    print("rank", rank, "ok", e1, e2, e3)
+    print("rank", rank, "ok", e1, e2, e3, e4)
 ''')
 
 
