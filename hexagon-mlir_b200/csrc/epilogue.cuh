@@ -431,7 +431,7 @@ __device__ __forceinline__ void epi_store_scalar(const EpiArgs &e, float v, int3
 }
 
 
-// Store of one full 32-column chunk for a whole warp through its 4 KB
+// Store (to C only) of one full 32-column chunk for a whole warp through its 4 KB
 // staging buffer `stg`: each thread parks its row segment in shared memory,
 // then the warp writes 8 rows x 64 B (16-bit C) or 4 rows x 128 B (32-bit C)
 // per store instruction instead of 32 rows x 16 B.  The 16-byte chunks of a
@@ -471,8 +471,6 @@ __device__ __forceinline__ void epi_store32_staged_t(const EpiArgs &e, const flo
       if (m0 + r < e.M) {
         const int64_t off = static_cast<int64_t>(m0 + r) * e.ldc + n0 + qq * 8;
         *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(e.C) + off) = x;
-        for (int t = 0; t < e.n_peers; ++t)  // fused all-gather: the same chunk to every peer
-          *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(e.peer_C[t]) + off) = x;
       }
     }
   } else {
@@ -501,8 +499,6 @@ __device__ __forceinline__ void epi_store32_staged_t(const EpiArgs &e, const flo
       if (m0 + r < e.M) {
         const int64_t off = static_cast<int64_t>(m0 + r) * e.ldc + n0 + qq * 4;
         *reinterpret_cast<uint4 *>(static_cast<uint32_t *>(e.C) + off) = x;
-        for (int t = 0; t < e.n_peers; ++t)  // fused all-gather: the same chunk to every peer
-          *reinterpret_cast<uint4 *>(static_cast<uint32_t *>(e.peer_C[t]) + off) = x;
       }
     }
   }

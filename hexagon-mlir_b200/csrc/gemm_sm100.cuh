@@ -246,7 +246,9 @@ __device__ __forceinline__ void epi_row_ct(const EpiArgs &e, uint32_t t_row, int
 template <int BN, int BN_OUT, int KIND, bool SWIGLU>
 __device__ __forceinline__ void epi_row(const EpiArgs &e, uint32_t t_row, int m, int n_base, int c0,
                                         Pre16 &pf, uint8_t *stg) {
-  if (!(e.pre16 && e.c_vec_ok && n_base + BN_OUT <= e.N)) {
+  // rows whose chunks also go to peers (fused all-gather) take the generic
+  // loop, which stores to every target; the specialised loop stores C only
+  if (!(e.pre16 && e.c_vec_ok && n_base + BN_OUT <= e.N) || e.n_peers > 0) {
     epi_row_generic<BN, BN_OUT, KIND, SWIGLU>(e, t_row, m, n_base, c0);
     return;
   }
@@ -718,7 +720,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const int n0 = n_blk * Cfg::kBNOut + oc * 32;
           if (!raw_int) epi_transform32(p.epi, v, up, m, n0);
-          if (p.epi.c_vec_ok && n0 + 32 <= p.epi.N)
+          if (p.epi.c_vec_ok && n0 + 32 <= p.epi.N && p.epi.n_peers == 0)
             epi_store32_staged_rt(p.epi, v, r, raw_int, m - lane, n0, stage_out + (warp - 2) * 4096);
           else
             epi_store32(p.epi, v, r, raw_int, m, n0);
