@@ -505,4 +505,57 @@ __device__ __forceinline__ void epi_store32_staged_t(const EpiArgs &e, const flo
   __syncwarp();  // the next chunk may overwrite stg
 }
 
+
+// Staged store of one full 32-column chunk to C and to every peer copy
+// (fused all-gather), for a whole warp; runtime output dtype.  The row
+// segments leave as whole 64 / 128-byte pieces, which matters more over
+// NVLink than locally.  Same preconditions as epi_store32_staged_t.
+inline __device__ __noinline__ void epi_store32_staged_all(const EpiArgs &e, const float (&v)[32],
+                                                    const uint32_t (&raw)[32], bool raw_int, int m0,
+                                                    int n0, uint8_t *stg) {
+  const int lane = threadIdx.x & 31;
+  const bool b16 = (e.c_dtype == HX_F16 || e.c_dtype == HX_BF16);
+  uint32_t w[32];
+  if (b16) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (e.c_dtype == HX_F16) {
+        __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+        w[j] = *reinterpret_cast<uint32_t *>(&h);
+      } else {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        w[j] = *reinterpret_cast<uint32_t *>(&h);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      w[j] = raw_int ? raw[j]
+                     : (e.c_dtype == HX_F32 ? __float_as_uint(v[j]) : static_cast<uint32_t>(__float2int_rn(v[j])));
+  }
+  const int row_bytes = b16 ? 64 : 128;     // bytes of the chunk in one row
+  const int cpr = row_bytes / 16;           // 16-byte pieces per row
+  const int esz = b16 ? 2 : 4;
+  uint8_t *row = stg + lane * row_bytes;
+  for (int q = 0; q < cpr; ++q) {
+    const int sw = b16 ? ((lane >> 1) & 3) : (lane & 7);
+    *reinterpret_cast<uint4 *>(row + ((q ^ sw) << 4)) = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  }
+  __syncwarp();
+  const int rpi = 32 / cpr;  // rows per warp instruction
+  const int qq = lane % cpr;
+  for (int i = 0; i < cpr; ++i) {
+    const int r = i * rpi + lane / cpr;
+    const int sw = b16 ? ((r >> 1) & 3) : (r & 7);
+    const uint4 x = *reinterpret_cast<const uint4 *>(stg + r * row_bytes + ((qq ^ sw) << 4));
+    if (m0 + r < e.M) {
+      const int64_t off = (static_cast<int64_t>(m0 + r) * e.ldc + n0) * esz + qq * 16;
+      *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(e.C) + off) = x;
+      for (int t = 0; t < e.n_peers; ++t)
+        *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(e.peer_C[t]) + off) = x;
+    }
+  }
+  __syncwarp();  // the next chunk may overwrite stg
+}
+
 }  // namespace hx

@@ -188,7 +188,8 @@ __device__ __forceinline__ void epi_row_t(const EpiArgs &e, uint32_t t_row, int 
 // Every other row (a partial last tile, unaligned C, 32-bit operands): the
 // runtime-dispatched epilogue and row stores, out of line.
 template <int BN, int BN_OUT, int KIND, bool SWIGLU>
-__device__ __noinline__ void epi_row_generic(const EpiArgs &e, uint32_t t_row, int m, int n_base, int c0) {
+__device__ __noinline__ void epi_row_generic(const EpiArgs &e, uint32_t t_row, int m, int n_base, int c0,
+                                             uint8_t *stg) {
   const bool raw_int = (KIND == 2) && (e.c_dtype == HX_S32) && (e.epi == HX_EPI_NONE);
 #pragma unroll 1
   for (int c = c0; c < BN_OUT / 32; c += 2) {
@@ -210,7 +211,10 @@ __device__ __noinline__ void epi_row_generic(const EpiArgs &e, uint32_t t_row, i
     }
     const int n0 = n_base + c * 32;
     if (!raw_int) epi_transform32(e, v, up, m, n0);
-    epi_store32(e, v, r, raw_int, m, n0);
+    if (e.n_peers > 0 && e.c_vec_ok && n0 + 32 <= e.N)  // fused all-gather: coalesced stores
+      epi_store32_staged_all(e, v, r, raw_int, m - static_cast<int>(threadIdx.x & 31), n0, stg);
+    else
+      epi_store32(e, v, r, raw_int, m, n0);
   }
 }
 
@@ -249,7 +253,7 @@ __device__ __forceinline__ void epi_row(const EpiArgs &e, uint32_t t_row, int m,
   // rows whose chunks also go to peers (fused all-gather) take the generic
   // loop, which stores to every target; the specialised loop stores C only
   if (!(e.pre16 && e.c_vec_ok && n_base + BN_OUT <= e.N) || e.n_peers > 0) {
-    epi_row_generic<BN, BN_OUT, KIND, SWIGLU>(e, t_row, m, n_base, c0);
+    epi_row_generic<BN, BN_OUT, KIND, SWIGLU>(e, t_row, m, n_base, c0, stg);
     return;
   }
   switch (e.c_dtype) {
