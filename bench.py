@@ -406,7 +406,7 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
     p2p = world > 1 and args.gather == "p2p"
     chunks = 4 if (world > 1 and not p2p and M % 4 == 0) else 1
     mc = M // chunks
-    gathered = torch.empty(chunks, world * mc, ns, dtype=odt, device=dev) if world > 1 else None
+    gathered = torch.empty(chunks, world * mc, ns, dtype=odt, device=dev) if (world > 1 and not p2p) else None
     side = torch.cuda.Stream(dev) if world > 1 else None
     main = torch.cuda.current_stream(dev)
     evs_c = [torch.cuda.Event() for _ in range(chunks)]
@@ -416,7 +416,16 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
 
     if p2p:
         from qcom_hexagon_backend.sharding import P2PGather
-        pg = P2PGather(M, ns, odt)
+        try:
+            pg = P2PGather(M, ns, odt)
+        except Exception as ex:  # peer mapping unavailable: NCCL all-gather instead
+            print(f"fused gather unavailable ({ex}); using NCCL", file=sys.stderr)
+            p2p = False
+            chunks = 4 if M % 4 == 0 else 1
+            mc = M // chunks
+            gathered = torch.empty(chunks, world * mc, ns, dtype=odt, device=dev)
+            side = torch.cuda.Stream(dev)
+            evs_c = [torch.cuda.Event() for _ in range(chunks)]
 
     def step():
         if world == 1:
@@ -524,7 +533,7 @@ def main(argv=None):
     ap.add_argument("--layers", type=int, default=22, help="decoder layers for --workload tinyllama")
     ap.add_argument("--chain", action="store_true",
                     help="stacks: run consecutive linears as one persistent launch (chain_gemms)")
-    ap.add_argument("--gather", choices=["p2p", "nccl"], default="nccl",
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
                     help="LM head at N>1: fused GEMM + NVLink all-gather (p2p) or GEMM + NCCL")
     ap.add_argument("--lm-dtype", choices=["bf16", "int8"], default="bf16",
                     help="LM head: bf16, or the int8 W8A8 variant (int32 accumulate)")
