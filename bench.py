@@ -1,19 +1,21 @@
 """Benchmark of the B200 linear-layer GEMM path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl hx|reference]
-                    [--workload gpt2|qwen|tinyllama|lmhead|cube]
+                    [--workload lmhead|gpt2|qwen|tinyllama] [--lm-dtype bf16|int8]
 
-Default workload (the configuration the headline metric is quoted on): the
-GPT-2-small linear stack, fp16, batch 1 x seq 1024, hidden 768, 12 layers
-(QKV +bias, attn-out +bias+residual, MLP-up +bias+GELU-tanh, MLP-down
-+bias+residual), random-init weights N(0,0.02), activations N(0,1).
+Default workload, at every N (the configuration the headline metric is
+quoted on at 1/2/4/8 GPUs): the LM-head GEMM, bf16, M=16384 tokens x
+K=2048 x N=50304, weights N(0,0.02), activations N(0,1), column-sharded
+over the N ranks.  A "step" is one pass of the sharded GEMM; at N > 1 it
+includes the all-gather of the logits onto every rank (by default fused
+into the GEMM's epilogue as stores over NVLink).  value = 2*M*N*K / step
+time (max over ranks), strong scaling.  The inputs (1.9 GB) exceed the
+126 MB L2, so no flush is needed between steps.
 
-A "step" is one forward of the whole stack (48 fused GEMM launches,
-173.95 GFLOP), replayed from a CUDA graph.  Each timed step is bracketed by
-CUDA events on the launching stream with a 256 MB L2 flush before it
-(outside the events).  Multi-GPU: one process per GPU under torchrun; the
-GPT-2/Qwen stacks run as independent replicas (weak scaling), the LM head
-is column-sharded over N (strong scaling).  Time is the max over ranks.
+The other workloads are BASELINE's configs 2-4: the GPT-2-small and
+Qwen2.5-0.5B linear stacks (CUDA-graph replays of the FX-compiled module,
+256 MB L2 flush before each step, replicas at N > 1) and the TinyLlama
+W8A16 decode step (one grouped persistent launch).
 
 --impl reference runs the reference's own CPU path for the same workload
 (PyTorch-CPU F.linear + epilogue in the config dtype, the golden every
@@ -180,10 +182,10 @@ def build_gpt2(dev, seed=1234):
     g = torch.Generator().manual_seed(seed)
     x = torch.randn(1024, 768, generator=g).half()
     launcher = TorchMLIRHexagonLauncher()
-    cg = launcher.compile_torch_mlir(model, [x], "gpt2_linear_stack",
-                                     HexagonOptions(device=dev.index, chain_gemms=CHAIN))
+    options = HexagonOptions(device=dev.index, chain_gemms=CHAIN)
+    cg = launcher.compile_torch_mlir(model, [x], "gpt2_linear_stack", options)
     flops = WL.gpt2_stack_flops()
-    return dict(launcher=launcher, model=model, cg=cg, x=x, flops=flops, launches=cg.n_hx_calls,
+    return dict(launcher=launcher, model=model, cg=cg, x=x, options=options, flops=flops, launches=cg.n_hx_calls,
                 metric="GEMM+epilogue TFLOP/s", unit="TFLOP/s", dtype="fp16",
                 config={"workload": "gpt2-small linear stack (BASELINE config 2)", "model": "gpt2-small-linears",
                         "layers": 12, "global_batch": 1, "seq_len": 1024, "hidden": 768,
@@ -198,10 +200,10 @@ def build_qwen(dev, seed=1235):
     g = torch.Generator().manual_seed(seed)
     x = torch.randn(2048, 896, generator=g).to(torch.bfloat16)
     launcher = TorchMLIRHexagonLauncher()
-    cg = launcher.compile_torch_mlir(model, [x], "qwen_linear_stack",
-                                     HexagonOptions(device=dev.index, chain_gemms=CHAIN))
+    options = HexagonOptions(device=dev.index, chain_gemms=CHAIN)
+    cg = launcher.compile_torch_mlir(model, [x], "qwen_linear_stack", options)
     flops = WL.qwen_stack_flops()
-    return dict(launcher=launcher, model=model, cg=cg, x=x, flops=flops, launches=cg.n_hx_calls,
+    return dict(launcher=launcher, model=model, cg=cg, x=x, options=options, flops=flops, launches=cg.n_hx_calls,
                 metric="GEMM+epilogue TFLOP/s", unit="TFLOP/s", dtype="bf16",
                 config={"workload": "qwen2.5-0.5b prefill linear stack (BASELINE config 3)",
                         "model": "qwen2.5-0.5b-linears", "layers": 24, "global_batch": 1, "seq_len": 2048,
@@ -253,7 +255,7 @@ def run_hx(args):
     x_host = W["x"].pin_memory()
     out_host = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in cg.static_out]
     for _ in range(2):
-        launcher.run_torch_mlir(W["model"], [x_host], W["func"], outputs=out_host)
+        launcher.run_torch_mlir(W["model"], [x_host], W["func"], options=W["options"], outputs=out_host)
     barrier(world, dev)
     stream = torch.cuda.current_stream(dev)
     e2e_ms = []
@@ -261,7 +263,7 @@ def run_hx(args):
         flush.zero_()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(stream)
-        launcher.run_torch_mlir(W["model"], [x_host], W["func"], outputs=out_host)
+        launcher.run_torch_mlir(W["model"], [x_host], W["func"], options=W["options"], outputs=out_host)
         e.record(stream)
         e.synchronize()
         e2e_ms.append(s.elapsed_time(e))
@@ -378,10 +380,12 @@ def run_tinyllama(args, world, rank, dev, peaks, peak_src):
 
 def run_lmhead(args, world, rank, dev, peaks, peak_src):
     """Config 5: LM head M=16384 x K=2048 x N=50304, bf16 (or int8 W8A8 with int32
-    accumulate, --lm-dtype int8), column-sharded over the ranks.  With N > 1 GPUs each
-    step also all-gathers the logits (NCCL over NVLink) into [world, M, N/world] on
-    every rank; the GEMM runs in M chunks and chunk c's all-gather, on a side stream,
-    overlaps chunk c+1's GEMM.  gemm_only reports the sharded GEMMs alone."""
+    accumulate, --lm-dtype int8), column-sharded over the ranks.  At N > 1 every step
+    also all-gathers the logits into [world, M, N/world] on every rank: by default the
+    GEMM's own epilogue stores each output chunk into every peer's buffer over NVLink
+    (one fused launch, hx_sharded_gemm_gather_p2p); --gather nccl runs the GEMM in M
+    chunks with chunk c's NCCL all-gather on a side stream overlapping chunk c+1.
+    gemm_only reports the sharded GEMM alone."""
     from qcom_hexagon_backend import ops
     from qcom_hexagon_backend.sharding import shard_range, shard_width
 
@@ -393,44 +397,43 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
     n0, n1 = shard_range(N, world, rank)
     g = torch.Generator().manual_seed(1238)
     if int8:
-        a = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8).to(dev)
+        a_cpu = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
         w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8)[n0:n1]
     else:
-        a = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
+        a_cpu = torch.randn(M, K, generator=g).to(torch.bfloat16)
         w = (torch.randn(N, K, generator=g)[n0:n1] * 0.02).to(torch.bfloat16)
     if w.shape[0] < ns:  # the short last shard: zero rows, equal gather sizes
         w = torch.cat([w, torch.zeros(ns - w.shape[0], K, dtype=w.dtype)], 0)
+    a = a_cpu.to(dev)
     w = w.contiguous().to(dev)
     odt = torch.int32 if int8 else torch.bfloat16
+    esz = 4 if int8 else 2
     out = torch.empty(M, ns, dtype=odt, device=dev)
     p2p = world > 1 and args.gather == "p2p"
-    chunks = 4 if (world > 1 and not p2p and M % 4 == 0) else 1
-    mc = M // chunks
-    gathered = torch.empty(chunks, world * mc, ns, dtype=odt, device=dev) if (world > 1 and not p2p) else None
-    side = torch.cuda.Stream(dev) if world > 1 else None
     main = torch.cuda.current_stream(dev)
-    evs_c = [torch.cuda.Event() for _ in range(chunks)]
 
     def gemm_only():
         ops.gemm(a, w, out=out)
 
+    pg = None
     if p2p:
         from qcom_hexagon_backend.sharding import P2PGather
-        try:
+        try:  # all ranks construct it or all raise (collective vote inside)
             pg = P2PGather(M, ns, odt)
-        except Exception as ex:  # peer mapping unavailable: NCCL all-gather instead
-            print(f"fused gather unavailable ({ex}); using NCCL", file=sys.stderr)
+        except RuntimeError as ex:
+            if rank == 0:
+                print(f"{ex}; using NCCL", file=sys.stderr)
             p2p = False
-            chunks = 4 if M % 4 == 0 else 1
-            mc = M // chunks
-            gathered = torch.empty(chunks, world * mc, ns, dtype=odt, device=dev)
-            side = torch.cuda.Stream(dev)
-            evs_c = [torch.cuda.Event() for _ in range(chunks)]
+    chunks = 4 if (world > 1 and not p2p and M % 4 == 0) else 1
+    mc = M // chunks
+    gathered = torch.empty(chunks, world * mc, ns, dtype=odt, device=dev) if (world > 1 and not p2p) else None
+    side = torch.cuda.Stream(dev) if (world > 1 and not p2p) else None
+    evs_c = [torch.cuda.Event() for _ in range(chunks)]
 
     def step():
         if world == 1:
             return gemm_only()
-        if p2p:  # one launch: the GEMM's epilogue writes every rank's buffer over NVLink
+        if p2p:  # one fused launch: the GEMM's epilogue writes every rank's buffer over NVLink
             pg.run(a, w)
             return
         for c in range(chunks):
@@ -440,6 +443,12 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
             with torch.cuda.stream(side):
                 dist.all_gather_into_tensor(gathered[c], out[c * mc:(c + 1) * mc])
         main.wait_stream(side)
+
+    def local_shard():
+        """This rank's [M, ns] logits after a step (its slot of the gather buffer)."""
+        if p2p:
+            return pg._local_view[rank]
+        return out
 
     def timed(fn, steps):
         evs = []
@@ -460,38 +469,108 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
     local_ms = timed(step, args.steps)
     clocks = clk.stop()
     total = max_over_ranks(local_ms, world, dev)
-    gemm_ms = max_over_ranks(timed(gemm_only, max(3, args.steps // 4)), world, dev) / max(3, args.steps // 4)
+    g_steps = max(3, args.steps // 4)
+    gemm_ms = max_over_ranks(timed(gemm_only, g_steps), world, dev) / g_steps
     ms = total / args.steps
     flops = 2.0 * M * N * K
     tflops = flops / (ms / 1e3) / 1e12
-    my_gemm_ms = gemm_ms
-    my_tflops = 2.0 * M * (n1 - n0) * K / (my_gemm_ms / 1e3) / 1e12
+
+    # e2e: host in, host out, every step.  A goes host->device from pinned
+    # memory, the step runs (GEMM + gather at N > 1), and this rank's column
+    # shard of the logits comes back device->host, so across ranks the full
+    # logits are read back once per step.
+    a_host = a_cpu.pin_memory()
+    out_host = torch.empty(M, ns, dtype=odt, pin_memory=True)
+
+    def e2e_step():
+        a.copy_(a_host, non_blocking=True)
+        step()
+        out_host.copy_(local_shard(), non_blocking=True)
+
+    e2e_step()
+    barrier(world, dev)
+    e2e_steps = max(3, min(args.steps, 20))
+    e2e_ms = []
+    for _ in range(e2e_steps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(main)
+        e2e_step()
+        e.record(main)
+        e.synchronize()
+        e2e_ms.append(s.elapsed_time(e))
+    e2e_total = max_over_ranks(sum(e2e_ms), world, dev)
+    e2e_value = flops / (e2e_total / e2e_steps / 1e3) / 1e12
+    h2d = a_host.numel() * a_host.element_size()
+    d2h = out_host.numel() * out_host.element_size()
+
     peak_key = "bf16_tflops"
     peak = float(peaks.get(peak_key, FALLBACK_PEAKS["bf16_tflops"])) * (2.0 if int8 else 1.0)
     unit = "TOP/s" if int8 else "TFLOP/s"
     dtname = "int8 (int32 acc)" if int8 else "bf16"
+    my_flops = 2.0 * M * (n1 - n0) * K
+    traffic = read_traffic("gemm_lmhead_int8.txt" if int8 else "gemm_lmhead.txt")
+    if traffic is not None and args.lm_rows:
+        traffic = None  # the recorded capture is of the full 16384-row launch
+    if world == 1:
+        # one GEMM launch per step: its average duration is the timed region's step time
+        per_launch = local_ms / args.steps
+        achieved = my_flops / (per_launch / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "kernel": "hx_gemm_sm100_2sm_kernel", "per_launch_ms": round(per_launch, 5),
+                "peak_source": f"{peak_src} {peak_key} (burst)" + (" x2 (int8 dense rate)" if int8 else "")}
+    else:
+        # A fused compute+collective step: its target time is the slower of the
+        # GEMM at the measured tensor peak and the bytes every rank must receive
+        # over NVLink at the measured 770 GB/s peer-copy rate.
+        recv = (world - 1) * M * ns * esz
+        t_tensor = my_flops / (peak * 1e12) * 1e3
+        t_link = recv / 770e9 * 1e3
+        target = max(t_tensor, t_link)
+        roof = {"bound": "nvlink" if t_link >= t_tensor else "tensor",
+                "achieved": round(recv / (ms / 1e3) / 1e9, 1) if t_link >= t_tensor else
+                round(my_flops / (ms / 1e3) / 1e12, 2),
+                "peak": 770.0 if t_link >= t_tensor else peak,
+                "unit": "GB/s" if t_link >= t_tensor else unit,
+                "frac": round(target / ms, 4), "traffic": traffic if p2p else None,
+                "target_ms": round(target, 4), "tensor_ms": round(t_tensor, 4), "nvlink_ms": round(t_link, 4),
+                "kernel": "hx_gemm_sm100_2sm_kernel (fused peer-store epilogue)" if p2p
+                else "hx_gemm_sm100_2sm_kernel + NCCL all-gather",
+                "peak_source": f"{peak_src} {peak_key} and measured 770 GB/s NVLink peer copy per direction"}
     line = {"metric": "GEMM+epilogue TFLOP/s", "value": round(tflops, 2), "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "int8" if int8 else "bf16", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8" if int8 else "bf16",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) random-init weights)",
             "config": {"workload": f"LM head {M}x2048x50304 {dtname}, column-sharded (BASELINE config 5)",
+                       "M": M, "K": K, "N": N, "shard_cols": ns,
                        "parallelism": f"tp{world} (N-sharded"
                        + ((", logits all-gathered into [world, M, N/world] by the GEMM's own epilogue "
                            "stores over NVLink (fused, hx_sharded_gemm_gather_p2p))" if p2p else
                            ", logits all-gathered over NCCL into [world, M, N/world], overlapped in "
                            f"{chunks} M-chunks)") if world > 1 else ")"),
-                       "l2": "inputs (1.9 GB/step) larger than L2"},
+                       "l2": "inputs (1.9 GB/step at N=1) larger than L2; no flush"},
             "gemm_only": {"value": round(flops / (gemm_ms / 1e3) / 1e12, 2), "unit": unit,
                           "ms_per_step": round(gemm_ms, 4)},
+            "e2e": {"value": round(e2e_value, 2), "unit": unit, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "api": ("sharding.P2PGather.run" if p2p else "ops.gemm" + (" + NCCL all-gather" if world > 1 else ""))
+                    + " with A copied from pinned host memory and this rank's logits shard copied back"},
             "gpu_launches": args.steps * (3 if p2p else chunks),
-            "roofline": {"bound": "tensor", "achieved": round(my_tflops, 2), "peak": peak, "unit": unit,
-                         "frac": round(my_tflops / peak, 4),
-                         "traffic": None if int8 else read_traffic("gemm_lmhead.txt"),
-                         "kernel": "hx_gemm_sm100_2sm_kernel",
-                         "peak_source": f"{peak_src} {peak_key}" + (" x2 (int8 dense rate)" if int8 else "")},
+            "roofline": roof,
             "clocks": clocks}
-    if p2p:
-        if int(pg.error_flag.item()) != 0:
-            line["error"] = f"fused gather error flag {int(pg.error_flag.item())}"
+    if world > 1:
+        recv = (world - 1) * M * ns * esz
+        line["gather"] = {"bytes_received_per_rank": recv,
+                          "nvlink_gbs_per_rank": round(recv / (ms / 1e3) / 1e9, 1),
+                          "gather_only_ms_est": round(max(0.0, ms - gemm_ms), 4),
+                          "reference_peer_copy_gbs": 770.0}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, u, sample, cores = cpu_reference_time("lmhead_int8" if int8 else "lmhead", budget_s=args.cpu_budget)
+        line["cpu_baseline"] = {"value": v, "unit": u, "cores": cores, "kind": "port", "sample": sample}
+    if pg is not None:
+        flag = int(pg.error_flag.item())
+        if flag != 0:
+            line["error"] = f"fused gather error flag {flag}"
         pg.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -508,11 +587,12 @@ def run_reference(args):
 
     n = cpu_threads()
     torch.set_num_threads(n)
-    vals = CR.run_steps(args.workload, steps=args.steps, warmup=args.warmup, threads=n,
+    wl = "lmhead_int8" if (args.workload == "lmhead" and args.lm_dtype == "int8") else args.workload
+    vals = CR.run_steps(wl, steps=args.steps, warmup=args.warmup, threads=n,
                         budget_s=args.cpu_budget)
     line = {"impl": "reference", "metric": vals["metric"], "value": vals["value"], "unit": vals["unit"],
             "n_gpus": int(os.environ.get("WORLD_SIZE", args.gpus)), "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": vals["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": vals["ms_per_step"], "higher_is_better": True, "scaling": vals.get("scaling", "weak"),
             "vs_baseline": None, "dtype": vals["dtype"], "data": "synthetic",
             "config": vals["config"],
             "cpu_baseline": {"value": vals["value"], "unit": vals["unit"], "cores": n, "kind": "port",
@@ -528,7 +608,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["hx", "reference"], default="hx")
-    ap.add_argument("--workload", choices=["gpt2", "qwen", "tinyllama", "lmhead"], default="gpt2")
+    ap.add_argument("--workload", choices=["gpt2", "qwen", "tinyllama", "lmhead"], default="lmhead")
     ap.add_argument("--batch", type=int, default=1, help="decode batch M for --workload tinyllama")
     ap.add_argument("--layers", type=int, default=22, help="decoder layers for --workload tinyllama")
     ap.add_argument("--chain", action="store_true",

@@ -560,11 +560,10 @@ int launch_w8a16_tc(const CUtensorMap &tw, const CUtensorMap &tx, const W8A16Par
                     cudaStream_t s) {
   auto kern = hx_w8a16_tc_kernel<MPAD>;
   const int smem = W8Cfg<MPAD>::smem_bytes(p.stages);
-  static std::atomic<int> configured{0};
-  if (!configured.load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+  static SmemAttrOnce attr_once;
+  {
+    cudaError_t e = ensure_max_smem(kern, attr_once);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w8a16)");
-    configured.store(1, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -807,12 +806,9 @@ int gemm_chain_impl(const hx_gemm_desc *descs, const int32_t *a_dep, const int32
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(chain counters)");
   auto kern = hx_gemm_chain_kernel<BN>;
   const int smem = p.stages * stage_bytes(BN) + 1024 + 256;
-  static std::atomic<int> configured{0};
-  if (!configured.load(std::memory_order_acquire)) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(chain)");
-    configured.store(1, std::memory_order_release);
-  }
+  static SmemAttrOnce attr_once;
+  e = ensure_max_smem(kern, attr_once);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(chain)");
   const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
   e = launch_pdl(kern, dim3(grid), dim3(kThreads), static_cast<size_t>(smem), s, p);
   if (e == cudaSuccess) e = cudaGetLastError();
@@ -868,15 +864,12 @@ int gemv_grouped_tc_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32
   cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int32_t) * count, s);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(counters)");
   const int grid = static_cast<int>(std::min<int64_t>(items, sms));
-  auto launch = [&](auto kern, int smem, std::atomic<int> &configured) -> cudaError_t {
-    if (!configured.load(std::memory_order_acquire)) {
-      cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (r != cudaSuccess) return r;
-      configured.store(1, std::memory_order_release);
-    }
+  auto launch = [&](auto kern, int smem, SmemAttrOnce &once) -> cudaError_t {
+    cudaError_t r = ensure_max_smem(kern, once, smem);
+    if (r != cudaSuccess) return r;
     return launch_pdl(kern, dim3(grid), dim3(kGtThreads), smem, s, p);
   };
-  static std::atomic<int> conf16{0}, conf32{0}, conf64{0};
+  static SmemAttrOnce conf16, conf32, conf64;
   if (M <= 16) e = launch(hx_gemv_w8a16_grouped_tc_kernel<16>, GtCfg<16>::kSmemBytes, conf16);
   else if (M <= 32) e = launch(hx_gemv_w8a16_grouped_tc_kernel<32>, GtCfg<32>::kSmemBytes, conf32);
   else e = launch(hx_gemv_w8a16_grouped_tc_kernel<64>, GtCfg<64>::kSmemBytes, conf64);

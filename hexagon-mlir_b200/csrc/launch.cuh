@@ -33,6 +33,33 @@ constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in limit per block on sm_100
 constexpr int kNeedsNoSplit = 1;     // internal: split-K clusters would not all be resident
 constexpr uint64_t kDefaultTimeout = 4000000000ull;  // ~2 s at 2 GHz
 
+// cudaFuncSetAttribute acts on the current device only, so a process that
+// drives several GPUs must set a kernel's dynamic shared-memory limit once per
+// device.  One SmemAttrOnce per kernel instantiation records, as a bit per
+// device ordinal, where the attribute has been set.
+struct SmemAttrOnce {
+  std::atomic<uint64_t> mask{0};
+};
+constexpr int kMaxDevices = 64;
+
+template <typename K>
+cudaError_t ensure_max_smem(K kern, SmemAttrOnce &once, int bytes = kMaxDynSmem) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = (dev >= 0 && dev < kMaxDevices) ? (1ull << dev) : 0;
+  if (bit && (once.mask.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) once.mask.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
+inline int current_device_ordinal() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+  return dev;
+}
+
 // Launch with programmatic stream serialization (PDL): the kernel may begin
 // while its predecessor finishes; it calls griddepcontrol.wait before its
 // first global-memory access, so ordering is unchanged.

@@ -19,12 +19,10 @@ int launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
   q.red_smem = (p.splits > 1 && Cfg::red_bytes(p.splits) + fixed <= kMaxDynSmem) ? 1 : 0;
   const int smem = std::max(ring, q.red_smem ? Cfg::red_bytes(p.splits) : 0) + fixed;
   if (smem > kMaxDynSmem) return unsupported("shared memory for this tile plan exceeds 227 KB");
-  static std::atomic<int> configured{0};
-  if (configured.load(std::memory_order_acquire) < smem) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kMaxDynSmem);
+  static SmemAttrOnce attr_once;
+  {
+    cudaError_t e = ensure_max_smem(kern, attr_once);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-    configured.store(kMaxDynSmem, std::memory_order_release);
   }
   cudaError_t e;
   if (p.splits > 1) {
@@ -44,12 +42,15 @@ int launch_tc(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
     cfg.numAttrs = 1;
     // Split-K runs one tile per cluster; clusters that do not all fit at once
     // would run as a second wave, so such plans fall back to no split.
-    static std::atomic<int> max_clusters[9];
-    int mc = max_clusters[p.splits].load(std::memory_order_acquire);
+    // The resident-cluster count depends on the device, so it is cached per ordinal.
+    static std::atomic<int> max_clusters[kMaxDevices][9];
+    const int dev = current_device_ordinal();
+    int mc = dev >= 0 ? max_clusters[dev][p.splits].load(std::memory_order_acquire) : 0;
     if (mc == 0) {
       e = cudaOccupancyMaxActiveClusters(&mc, kern, &cfg);
       if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
-      max_clusters[p.splits].store(std::max(mc, 1), std::memory_order_release);
+      mc = std::max(mc, 1);
+      if (dev >= 0) max_clusters[dev][p.splits].store(mc, std::memory_order_release);
     }
     if (grid / p.splits > mc) return kNeedsNoSplit;
     cfg.numAttrs = 2;
@@ -69,11 +70,10 @@ int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &
   const int stage = p.kbs * (kBM * kKBytes + (BN / 2) * kKBytes);
   const int smem = p.stages * stage + 1024 + kBarBytes + kStageOutBytes;
   if (smem > kMaxDynSmem) return unsupported("shared memory for this pair plan exceeds 227 KB");
-  static std::atomic<int> configured{0};
-  if (!configured.load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+  static SmemAttrOnce attr_once;
+  {
+    cudaError_t e = ensure_max_smem(kern, attr_once);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pair)");
-    configured.store(1, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);

@@ -61,7 +61,7 @@ def run_matmul(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, n_rows: int, n
             raise ValueError(f"{name} must be a torch.Tensor")
         if tuple(t.shape) != shape:
             raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {shape}")
-    dev = torch.device("cuda", opts.device if opts.device is not None else torch.cuda.current_device())
+    dev = opts.cuda_device()
     tile_n, stages = opts.tile_override()
     a = A.to(dev).contiguous()
     b = B.to(dev).contiguous()

@@ -41,7 +41,10 @@ class HexagonOptions:
     vectorize: int = 1
     vector_length: int = 32
     num_threads: int = 4
-    data_layout: str = ""
+    data_layout: str = (
+        "e-m:e-p:32:32:32-a:0-n16:32-i64:64:64-i32:32:32-i16:16:16-i1:8:8-f32:32:"
+        "32-f64:64:64-v32:32:32-v64:64:64-v512:512:512-v1024:1024:1024-v2048:2048:2048"
+    )
     num_warps: int = 1
     num_stages: int = 1
     num_ctas: int = 1
@@ -81,12 +84,13 @@ class HexagonOptions:
     LWPloopDepth: int = 1
 
     # ---- B200 additions ----
-    device: int = 0                 # CUDA device index
+    device: int = -1                # CUDA device index; -1 = the current device at compile time
     fuse_epilogue: bool = True      # fold bias/GELU/SiLU/SwiGLU/residual into the GEMM
     use_cuda_graph: bool = True     # capture the compiled graph's launches once, replay
     chain_gemms: bool = False       # run consecutive linears as one persistent launch
     world_size: int = 1             # column-sharding degree (LM-head style GEMMs)
     shard_dim: str = "n"            # only "n" (output columns) is supported
+    capture: str = "auto"           # FX capture: "trace", "export" (torch.export, aten ops) or "auto"
 
     def __post_init__(self):
         valid_artifacts = {"o", "llir", "so"}
@@ -99,7 +103,15 @@ class HexagonOptions:
             raise ValueError("shard_dim must be 'n' (column sharding)")
         if self.world_size < 1:
             raise ValueError("world_size must be >= 1")
+        if self.capture not in ("auto", "trace", "export"):
+            raise ValueError("capture must be 'auto', 'trace' or 'export'")
         self.tile_override()  # validates tileSizes
+
+    def cuda_device(self):
+        """The torch.device this configuration runs on (device -1: torch's current device)."""
+        import torch
+
+        return torch.device("cuda", self.device if self.device >= 0 else torch.cuda.current_device())
 
     def tile_override(self) -> Tuple[int, int]:
         """(tile_n, stages) from tileSizes; 0 means automatic."""

@@ -46,14 +46,24 @@ class TestReport:
         return f"Name:{self.name} Result:{self.result} Perf:{self.perf:.3f} Units:{self.units}"
 
 
+def _leaves(out) -> list:
+    """The forward's output tensors in pytree order (tuples, lists, dicts and
+    HF ModelOutput all flatten; the reference's launcher likewise returns the
+    flat list of the function's results, logits first for GPT2LMHeadModel)."""
+    import torch.utils._pytree as pytree
+
+    return [t for t in pytree.tree_leaves(out) if isinstance(t, torch.Tensor)]
+
+
 class CompiledGraph:
     """A model compiled for one input signature: rewritten FX module, static
     device buffers, and (optionally) the CUDA graph of one forward."""
 
     def __init__(self, module: nn.Module, example_inputs: Sequence[torch.Tensor], options: HexagonOptions):
         self.options = options
-        self.device = torch.device("cuda", options.device)
-        self.gm = fx_backend.compile_module(module, self.device, chain=options.chain_gemms)
+        self.device = options.cuda_device()
+        self.gm = fx_backend.compile_module(module, self.device, chain=options.chain_gemms,
+                                            example_inputs=example_inputs, mode=options.capture)
         self.n_hx_calls = fx_backend.count_hx_calls(self.gm)
         self.static_in = [torch.empty(t.shape, dtype=t.dtype, device=self.device) for t in example_inputs]
         for s, t in zip(self.static_in, example_inputs):
@@ -72,7 +82,7 @@ class CompiledGraph:
                 self.graph = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(self.graph, stream=self.stream):
                     out = self._forward()
-        self.static_out = list(out) if isinstance(out, (tuple, list)) else [out]
+        self.static_out = _leaves(out)
 
     def _forward(self):
         if self.options.chain_gemms:
@@ -85,8 +95,7 @@ class CompiledGraph:
         if self.graph is not None:
             self.graph.replay()
         else:
-            outs = self._forward()
-            outs = list(outs) if isinstance(outs, (tuple, list)) else [outs]
+            outs = _leaves(self._forward())
             for s, o in zip(self.static_out, outs):
                 s.copy_(o)
 
@@ -125,7 +134,7 @@ class TorchMLIRHexagonLauncher:
         if not isinstance(model, nn.Module):
             raise TypeError("model must be a torch.nn.Module")
         opts = options if isinstance(options, HexagonOptions) else HexagonOptions.from_dict(options)
-        key = (id(model), func_name, opts.hash(),
+        key = (id(model), func_name, opts.hash(), opts.cuda_device().index,
                tuple((tuple(t.shape), t.dtype) for t in inputs))
         cg = self._cache.get(key)
         if cg is None:

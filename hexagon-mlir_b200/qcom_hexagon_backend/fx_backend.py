@@ -4,16 +4,27 @@ to the B200 kernels.
 The reference takes a PyTorch model through torch-mlir
 (`torch_mlir.fx.export_and_import(..., LINALG_ON_TENSORS)`,
 benchmark_models/run_gpt2lmheadmodel.py:70-88), which turns each
-aten.linear / aten.addmm into linalg.transpose + linalg.matmul + an
+aten.linear / aten.addmm / aten.mm into linalg.transpose + linalg.matmul + an
 elementwise linalg.generic, then folds the transpose into
 matmul_transpose_b (lib/Transforms/ScheduleMatmulForHVXPass.cpp:84-93).
-Here the same graph-level decision is made on a torch.fx graph: each
-linear node, together with the elementwise op that consumes it, becomes one
-call of the fused GEMM kernel.
+Here the same graph-level decision is made on a torch.fx graph, either a
+symbolic trace (torch-level ops) or a torch.export graph (aten ops, the
+graph export_and_import starts from): each linear node, together with the
+elementwise op that consumes it, becomes one call of the fused GEMM kernel.
 
-Patterns (the producer must have the consumer as its only user):
+Linear nodes: F.linear / nn.Linear / aten.linear (W[N,K]); torch.addmm /
+aten.addmm (bias + x @ W[K,N], beta = alpha = 1, as HF Conv1D computes);
+torch.mm / aten.mm / torch.matmul / aten.matmul / `@` with a 2-D right
+operand (x @ W[K,N]).  A constant W[K,N] (a module parameter or buffer) is
+transposed once at compile time into a W[N,K] buffer, the transpose fold of
+ScheduleMatmulForHVXPass; a non-constant one runs as the B[K,N] layout.
+
+Epilogue patterns (each intermediate node must have one user).  Between
+the linear and its consumer the rewriter looks through views / reshapes and
+inference-mode dropout, which it re-applies to the fused result:
   linear(x)                          -> hx linear (bias if present)
   gelu(linear(x), approximate=tanh)  -> bias + GELU-tanh epilogue
+  0.5*y*(1+tanh(c*(y+0.044715*y^3))) -> the same (HF NewGELU written out)
   silu(linear(x))                    -> bias + SiLU epilogue
   linear(x) + r   /   r + linear(x)  -> bias + residual epilogue
   silu(linear_g(x)) * linear_u(x)    -> SwiGLU epilogue over [W_g; W_u]
@@ -24,6 +35,7 @@ Everything else in the graph runs unchanged (on the GPU, as torch ops).
 from __future__ import annotations
 
 import copy
+import math
 import operator
 from typing import Callable, Optional
 
@@ -34,25 +46,42 @@ import torch.nn.functional as F
 
 from . import ops
 
-_LINEAR_FNS = (F.linear, torch._C._nn.linear)
-_GELU_FNS = (F.gelu, torch._C._nn.gelu)
-_SILU_FNS = (F.silu,)
-_ADD_FNS = (operator.add, torch.add, operator.iadd)
-_MUL_FNS = (operator.mul, torch.mul)
+aten = torch.ops.aten
+_LINEAR_FNS = (F.linear, torch._C._nn.linear, aten.linear.default)
+_ADDMM_FNS = (torch.addmm, aten.addmm.default)
+_MM_FNS = (torch.mm, aten.mm.default)
+_MATMUL_FNS = (torch.matmul, operator.matmul, aten.matmul.default)
+_GELU_FNS = (F.gelu, torch._C._nn.gelu, aten.gelu.default)
+_SILU_FNS = (F.silu, aten.silu.default)
+_ADD_FNS = (operator.add, torch.add, operator.iadd, aten.add.Tensor)
+_MUL_FNS = (operator.mul, torch.mul, aten.mul.Tensor)
+_TANH_FNS = (torch.tanh, aten.tanh.default)
+_POW_FNS = (torch.pow, operator.pow, aten.pow.Tensor_Scalar)
+_VIEW_FNS = (aten.view.default, aten.reshape.default, aten._unsafe_view.default, aten.alias.default,
+             torch.reshape)
+_VIEW_METHODS = ("view", "reshape")
+_DROPOUT_FNS = (F.dropout, aten.dropout.default)
 
 
-def hx_linear(x, weight, bias=None, residual=None, activation=None, weight_const=False):
+def hx_linear(x, weight, bias=None, residual=None, activation=None, weight_const=False, b_layout="nk"):
     """Fused linear used as the call_function target of rewritten nodes.
+    weight: W[N,K] (b_layout "nk") or B[K,N] ("kn").  residual may have any
+    shape whose last dimension is N and whose size is x's rows x N (the
+    rewriter passes the consumer's operand, which can be the viewed shape).
     weight_const: the weight is a module parameter/buffer (constant while the
     compiled forward runs), so the kernel may prefetch it early."""
     if residual is not None:
-        out_shape = (*x.shape[:-1], weight.shape[0])
-        if tuple(residual.shape) != out_shape or residual.dtype != x.dtype:
-            # Broadcasting residual: not an epilogue the kernel fuses.
-            y = ops.linear(x, weight, bias, activation=activation, b_const=weight_const)
+        n = weight.shape[0] if b_layout == "nk" else weight.shape[1]
+        rows = x.numel() // x.shape[-1] if x.shape[-1] else 0
+        if residual.shape[-1] != n or residual.numel() != rows * n or residual.dtype != x.dtype \
+                or not residual.is_contiguous():
+            # Broadcasting or strided residual: not an epilogue the kernel fuses.
+            y = ops.linear(x, weight, bias, activation=activation, b_const=weight_const, b_layout=b_layout)
             ops.chain_flush()  # the add below reads y
-            return y + residual
-    return ops.linear(x, weight, bias, activation=activation, residual=residual, b_const=weight_const)
+            return y + residual.reshape(y.shape) if residual.numel() == y.numel() else y + residual
+        residual = residual.reshape(*x.shape[:-1], n)
+    return ops.linear(x, weight, bias, activation=activation, residual=residual, b_const=weight_const,
+                      b_layout=b_layout)
 
 
 def hx_swiglu(x, weight_gate_up):
@@ -65,10 +94,39 @@ def _users(n: fx.Node):
 
 
 class _LinearSite:
-    """A linear call in the graph: its input node and weight / bias sources."""
+    """A linear call in the graph: its input node, weight / bias sources and
+    the weight's layout ("nk" = W[N,K], "kn" = B[K,N])."""
 
-    def __init__(self, node, x, weight, bias):
-        self.node, self.x, self.weight, self.bias = node, x, weight, bias
+    def __init__(self, node, x, weight, bias, layout="nk"):
+        self.node, self.x, self.weight, self.bias, self.layout = node, x, weight, bias, layout
+
+
+def _rank(gm, v) -> Optional[int]:
+    """Tensor rank of a graph value when known (export metadata or a parameter)."""
+    if isinstance(v, fx.Node):
+        val = v.meta.get("val", v.meta.get("example_value"))
+        if isinstance(val, torch.Tensor):
+            return val.dim()
+        if v.op == "get_attr":
+            try:
+                t = _get_attr(gm, v.target)
+            except AttributeError:
+                return None
+            return t.dim() if isinstance(t, torch.Tensor) else None
+    return None
+
+
+def _get_attr(gm, qualname):
+    obj = gm
+    for part in qualname.split("."):
+        obj = getattr(obj, part)
+    return obj
+
+
+def _weight_src(w):
+    if isinstance(w, fx.Node) and w.op == "get_attr":
+        return ("attr", w.target)
+    return ("node", w)
 
 
 def _as_linear(gm: fx.GraphModule, n: fx.Node) -> Optional[_LinearSite]:
@@ -77,11 +135,46 @@ def _as_linear(gm: fx.GraphModule, n: fx.Node) -> Optional[_LinearSite]:
         if isinstance(mod, nn.Linear) and len(n.args) == 1 and not n.kwargs:
             return _LinearSite(n, n.args[0], ("attr", n.target + ".weight"),
                                ("attr", n.target + ".bias") if mod.bias is not None else None)
-    if n.op == "call_function" and n.target in _LINEAR_FNS:
+        return None
+    if n.op != "call_function":
+        return None
+    if n.target in _LINEAR_FNS:
         args = list(n.args) + [None] * (3 - len(n.args))
         x, w, b = args[0], n.kwargs.get("weight", args[1]), n.kwargs.get("bias", args[2])
-        return _LinearSite(n, x, ("node", w), ("node", b) if b is not None else None)
+        return _LinearSite(n, x, _weight_src(w), _weight_src(b) if b is not None else None)
+    if n.target in _ADDMM_FNS:
+        if len(n.args) != 3 or any(n.kwargs.get(k, 1) != 1 for k in ("beta", "alpha")):
+            return None
+        if set(n.kwargs) - {"beta", "alpha"}:
+            return None
+        b, x, w = n.args
+        if _rank(gm, b) not in (None, 1) or _rank(gm, w) not in (None, 2):
+            return None
+        return _LinearSite(n, x, _weight_src(w), _weight_src(b), "kn")
+    if n.target in _MM_FNS or n.target in _MATMUL_FNS:
+        if len(n.args) != 2 or n.kwargs:
+            return None
+        x, w = n.args
+        rw, rx = _rank(gm, w), _rank(gm, x)
+        if n.target in _MATMUL_FNS and (rw != 2 or rx is None or rx < 2):
+            return None  # only x[..., K] @ W[K, N]; batched products are not linears
+        return _LinearSite(n, x, _weight_src(w), None, "kn")
     return None
+
+
+def _is_transparent(gm, n: fx.Node) -> bool:
+    """A node that only reshapes its first input, or is inference-mode dropout."""
+    if n.op == "call_function" and n.target in _VIEW_FNS:
+        return True
+    if n.op == "call_method" and n.target in _VIEW_METHODS:
+        return True
+    if n.op == "call_function" and n.target in _DROPOUT_FNS:
+        train = n.kwargs.get("train", n.kwargs.get("training", n.args[2] if len(n.args) > 2 else
+                                                    (n.target is F.dropout)))
+        return train is False
+    if n.op == "call_module" and isinstance(gm.get_submodule(n.target), nn.Dropout):
+        return not gm.get_submodule(n.target).training
+    return False
 
 
 def _is_gelu_tanh(n: fx.Node) -> bool:
@@ -98,6 +191,73 @@ def _is_silu(gm, n: fx.Node) -> bool:
     return False
 
 
+def _fn(n, fns):
+    return isinstance(n, fx.Node) and n.op == "call_function" and n.target in fns and not n.kwargs
+
+
+def _scalar_pair(n: fx.Node, fns, value, tol=1e-6):
+    """(tensor operand) if n is fn(t, value) or fn(value, t) with a Python scalar."""
+    if not _fn(n, fns) or len(n.args) != 2:
+        return None
+    a, b = n.args
+    for t, c in ((a, b), (b, a)):
+        if isinstance(t, fx.Node) and isinstance(c, (int, float)) and abs(c - value) <= tol * max(1.0, abs(value)):
+            return t
+    return None
+
+
+def _gelu_tanh_expr(y: fx.Node) -> Optional[tuple]:
+    """Match 0.5*y*(1 + tanh(sqrt(2/pi)*(y + 0.044715*y^3))) written with
+    elementwise ops (HF NewGELUActivation / gelu_new), grouped as
+    (0.5*y)*(1 + tanh(...)), scalars on either side.  Returns (final node,
+    the expression's nodes) or None."""
+    users = _users(y)
+    if len(users) != 3:
+        return None
+    half = cube = inner = None
+    for u in users:
+        if _scalar_pair(u, _MUL_FNS, 0.5) is y:
+            half = u
+        elif _scalar_pair(u, _POW_FNS, 3.0) is y:
+            cube = u
+        elif _fn(u, _ADD_FNS) and len(u.args) == 2 and y in u.args:
+            inner = u
+    if half is None or cube is None or inner is None:
+        return None
+    nodes = [half, cube, inner]
+    cu = _users(cube)
+    if len(cu) != 1 or _scalar_pair(cu[0], _MUL_FNS, 0.044715) is not cube:
+        return None
+    k = cu[0]
+    nodes.append(k)
+    if k not in inner.args:
+        return None
+    iu = _users(inner)
+    if len(iu) != 1 or _scalar_pair(iu[0], _MUL_FNS, math.sqrt(2.0 / math.pi), 1e-5) is not inner:
+        return None
+    sc = iu[0]
+    nodes.append(sc)
+    su = _users(sc)
+    if len(su) != 1 or not (_fn(su[0], _TANH_FNS) and su[0].args[0] is sc):
+        return None
+    th = su[0]
+    nodes.append(th)
+    tu = _users(th)
+    if len(tu) != 1 or _scalar_pair(tu[0], _ADD_FNS, 1.0) is not th:
+        return None
+    one = tu[0]
+    nodes.append(one)
+    ou = _users(one)
+    hu = _users(half)
+    if len(ou) != 1 or len(hu) != 1 or ou[0] is not hu[0]:
+        return None
+    fin = ou[0]
+    if not (_fn(fin, _MUL_FNS) and set(fin.args) == {half, one}):
+        return None
+    nodes.append(fin)
+    return fin, nodes
+
+
 def _src(graph: fx.Graph, src):
     """Materialise a weight/bias source as a node."""
     if src is None:
@@ -106,17 +266,26 @@ def _src(graph: fx.Graph, src):
     return graph.get_attr(val) if kind == "attr" else val
 
 
-def rewrite(gm: fx.GraphModule) -> fx.GraphModule:
-    """Rewrite linear(+epilogue) patterns in place; returns the module."""
-    graph = gm.graph
-    sites = {}
-    for n in list(graph.nodes):
-        s = _as_linear(gm, n)
-        if s is not None:
-            sites[n] = s
-    done = set()
+def _has_param(gm, qualname):
+    try:
+        t = _get_attr(gm, qualname)
+    except AttributeError:
+        return False
+    return isinstance(t, torch.Tensor)
 
-    # SwiGLU: mul(silu(lin_g(x)), lin_u(x)), both bias-free, weights constant.
+
+def _transposed_const(gm, qualname, cache):
+    """Register (once) W[N,K] = B[K,N]^T for a constant weight; returns its attribute name."""
+    if qualname not in cache:
+        name = f"_hx_wT{len(cache)}"
+        gm.register_buffer(name, _get_attr(gm, qualname).detach().t().contiguous())
+        cache[qualname] = name
+    return cache[qualname]
+
+
+def _fuse_swiglu(gm: fx.GraphModule, sites: dict, done: set) -> None:
+    """mul(silu(lin_g(x)), lin_u(x)), both bias-free W[N,K] constants -> one SwiGLU GEMM."""
+    graph = gm.graph
     fused_count = 0
     for n in list(graph.nodes):
         if not (n.op == "call_function" and n.target in _MUL_FNS and len(n.args) == 2):
@@ -133,11 +302,12 @@ def rewrite(gm: fx.GraphModule) -> fx.GraphModule:
             sg, su = sites[lin_g], sites[lin_u]
             if sg.x is not su.x or sg.bias or su.bias or len(_users(lin_g)) != 1 or len(_users(lin_u)) != 1:
                 continue
-            if sg.weight[0] != "attr" or su.weight[0] != "attr":
+            if sg.weight[0] != "attr" or su.weight[0] != "attr" or sg.layout != "nk" or su.layout != "nk":
                 continue
-            wg = gm.get_parameter(sg.weight[1]) if _has_param(gm, sg.weight[1]) else None
-            wu = gm.get_parameter(su.weight[1]) if _has_param(gm, su.weight[1]) else None
-            if wg is None or wu is None or wg.shape != wu.shape:
+            if not (_has_param(gm, sg.weight[1]) and _has_param(gm, su.weight[1])):
+                continue
+            wg, wu = _get_attr(gm, sg.weight[1]), _get_attr(gm, su.weight[1])
+            if wg.shape != wu.shape:
                 continue
             name = f"_hx_swiglu_w{fused_count}"
             fused_count += 1
@@ -151,36 +321,81 @@ def rewrite(gm: fx.GraphModule) -> fx.GraphModule:
             done.update((lin_g, lin_u))
             break
 
+
+def _consumer(gm, cur: fx.Node):
+    """The epilogue that consumes `cur`: (activation, residual, tail, nodes) or None."""
+    us = _users(cur)
+    if len(us) == 1:
+        u = us[0]
+        if _is_gelu_tanh(u) and u.args[0] is cur:
+            return "gelu_tanh", None, u, [u]
+        if _is_silu(gm, u) and u.args and u.args[0] is cur:
+            return "silu", None, u, [u]
+        if (u.op == "call_function" and u.target in _ADD_FNS and len(u.args) == 2 and not u.kwargs):
+            other = u.args[1] if u.args[0] is cur else u.args[0]
+            if isinstance(other, fx.Node) and other is not cur:
+                return None, other, u, [u]
+    elif len(us) == 3:
+        m = _gelu_tanh_expr(cur)
+        if m is not None:
+            return "gelu_tanh", None, m[0], m[1]
+    return None
+
+
+def rewrite(gm: fx.GraphModule) -> fx.GraphModule:
+    """Rewrite linear(+epilogue) patterns in place; returns the module."""
+    graph = gm.graph
+    sites = {}
+    for n in list(graph.nodes):
+        s = _as_linear(gm, n)
+        if s is not None:
+            sites[n] = s
+    done = set()
+    _fuse_swiglu(gm, sites, done)
+    tcache = {}
     for n in list(sites):
         if n in done:
             continue
         s = _as_linear(gm, n)  # re-read: earlier rewrites may have replaced its inputs
-        users = _users(n)
-        act, residual, tail = None, None, n
-        if len(users) == 1:
-            u = users[0]
-            if _is_gelu_tanh(u):
-                act, tail = "gelu_tanh", u
-            elif _is_silu(gm, u):
-                act, tail = "silu", u
-            elif u.op == "call_function" and u.target in _ADD_FNS and len(u.args) == 2 and not u.kwargs:
-                other = u.args[1] if u.args[0] is n else u.args[0]
-                if isinstance(other, fx.Node) and other is not n:
-                    residual, tail = other, u
+        if s is None:
+            continue
+        chain, cur = [], n
+        while True:  # views / reshapes / inference dropout between the linear and its consumer
+            us = _users(cur)
+            if len(us) == 1 and _is_transparent(gm, us[0]) and us[0].args and us[0].args[0] is cur:
+                cur = us[0]
+                chain.append(cur)
+            else:
+                break
+        c = _consumer(gm, cur)
+        act, residual, tail, expr = c if c is not None else (None, None, cur, [])
         with graph.inserting_before(tail):
-            w = _src(graph, s.weight)
+            layout = s.layout
+            if s.weight[0] == "attr" and layout == "kn" and _has_param(gm, s.weight[1]):
+                w = graph.get_attr(_transposed_const(gm, s.weight[1], tcache))
+                layout = "nk"
+            else:
+                w = _src(graph, s.weight)
             b = _src(graph, s.bias)
             kwargs = {}
             if s.weight[0] == "attr":
                 kwargs["weight_const"] = True
+            if layout != "nk":
+                kwargs["b_layout"] = layout
             if act:
                 kwargs["activation"] = act
             if residual is not None:
                 kwargs["residual"] = residual
             new = graph.call_function(hx_linear, (s.x, w, b), kwargs)
-        tail.replace_all_uses_with(new)
-        if tail is not n:
-            graph.erase_node(tail)
+            mapping, last = {n: new}, new
+            for cn in chain:  # re-apply the reshapes to the fused result
+                last = graph.node_copy(cn, lambda a: mapping.get(a, a))
+                mapping[cn] = last
+        tail.replace_all_uses_with(last)
+        for dead in reversed(expr):
+            graph.erase_node(dead)
+        for dead in reversed(chain):
+            graph.erase_node(dead)
         graph.erase_node(n)
     graph.lint()
     gm.recompile()
@@ -205,26 +420,43 @@ def insert_chain_flushes(gm: fx.GraphModule) -> fx.GraphModule:
     return gm
 
 
-def _has_param(gm, qualname):
-    try:
-        gm.get_parameter(qualname)
-        return True
-    except AttributeError:
-        return False
-
-
 def count_hx_calls(gm: fx.GraphModule) -> int:
     return sum(1 for n in gm.graph.nodes if n.op == "call_function" and n.target in (hx_linear, hx_swiglu))
 
 
+def capture(module: nn.Module, example_inputs=None, mode: str = "auto") -> fx.GraphModule:
+    """The module as an FX graph.  "trace": torch.fx.symbolic_trace (torch-level
+    ops); "export": torch.export (aten ops, the graph torch-mlir's
+    export_and_import lowers); "auto": trace, and export when the module does
+    not trace (data-dependent Python, as in HF transformers models).  Export
+    needs example inputs on the module's device, since it records the devices
+    of tensors the forward creates."""
+    if mode not in ("auto", "trace", "export"):
+        raise ValueError("capture mode must be 'auto', 'trace' or 'export'")
+    if mode in ("auto", "trace"):
+        try:
+            return fx.symbolic_trace(module)
+        except Exception:  # noqa: BLE001 - untraceable Python control flow
+            if mode == "trace":
+                raise
+    if example_inputs is None:
+        raise ValueError("torch.export capture needs example inputs")
+    with torch.no_grad():
+        ep = torch.export.export(module, tuple(example_inputs))
+    return ep.module()
+
+
 def compile_module(module: nn.Module, device: torch.device | str = "cuda",
-                   chain: bool = False) -> fx.GraphModule:
-    """Trace `module`, move its parameters to `device` and rewrite its linear
+                   chain: bool = False, example_inputs=None, mode: str = "auto") -> fx.GraphModule:
+    """Capture `module` (see capture()), on `device`, and rewrite its linear
     layers onto the B200 kernels.  With `chain`, flush points are inserted so
     the graph can run under ops.chained() (consecutive linears become one
     hx_gemm_chain launch).  The original module is not modified."""
-    gm = fx.symbolic_trace(copy.deepcopy(module))  # the GraphModule would share parameters
-    gm = gm.to(device)
+    mod = copy.deepcopy(module).to(device)  # the GraphModule would share parameters
+    ex = None
+    if example_inputs is not None:
+        ex = [t.to(device) if isinstance(t, torch.Tensor) else t for t in example_inputs]
+    gm = capture(mod, ex, mode).to(device)
     gm = rewrite(gm)
     return insert_chain_flushes(gm) if chain else gm
 

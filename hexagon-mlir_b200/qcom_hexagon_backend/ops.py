@@ -298,11 +298,13 @@ def linear(
     activation: Optional[str] = None,
     residual: Optional[torch.Tensor] = None,
     out: Optional[torch.Tensor] = None,
+    b_layout: str = "nk",
     **kw,
 ) -> torch.Tensor:
     """nn.Linear forward with a fused epilogue: act(x @ W.T + bias) + residual.
 
     activation: None | "gelu_tanh" | "silu" | "swiglu" (weight = [gate; up]).
+    b_layout "kn" takes the weight as B[K,N] (x @ B + bias, aten.addmm's form).
     Leading dimensions of x are flattened, as aten.linear does.
     """
     lead = x.shape[:-1]
@@ -332,7 +334,9 @@ def linear(
     else:
         raise ValueError(f"unknown activation {activation!r}")
     o2 = out.reshape(-1, out.shape[-1]) if out is not None else None
-    y = gemm(x2, weight, b_layout="nk", out=o2, epilogue=epi, bias=bias, residual=r2, **kw)
+    if b_layout == "kn" and activation == "swiglu":
+        raise ValueError("swiglu takes the weight as [gate; up] W[2N,K]")
+    y = gemm(x2, weight, b_layout=b_layout, out=o2, epilogue=epi, bias=bias, residual=r2, **kw)
     return y.reshape(*lead, y.shape[-1])
 
 

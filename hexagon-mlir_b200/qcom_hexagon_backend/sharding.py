@@ -147,6 +147,11 @@ class P2PGather:
     all ranks' buffers at [rank], so when it returns (stream-ordered) the
     buffer holds every rank's shard.  All ranks must call run() the same
     number of times (it synchronises them on the GPU, with bounded waits).
+
+    If a bounded wait runs out, error_flag reads 41 and the contents of every
+    rank's gather buffer are undefined for that call: the GEMM still runs and
+    still stores into the peers' buffers, which a late peer may be reading.
+    The caller should treat the gather as failed on all ranks.
     """
 
     def __init__(self, M: int, ns: int, dtype: torch.dtype, group=None):
@@ -159,38 +164,72 @@ class P2PGather:
         esz = torch.empty(0, dtype=dtype).element_size()
         hsz = lib.hx_peer_handle_size()
         self._mine = []
+        self._opened = []
         handles = []
-        for nbytes in (self.world * M * ns * esz, 256):  # gather buffer, flags
-            ptr, h = ctypes.c_void_p(), (ctypes.c_uint8 * hsz)()
-            _lib.check(lib.hx_peer_alloc(nbytes, ctypes.byref(ptr), h), "hx_peer_alloc")
-            self._mine.append(ptr.value)
-            handles.append(bytes(h))
+        # Every step that can fail on one rank alone is followed by a
+        # collective vote, so either all ranks construct the gather or all
+        # raise: a rank that fell back alone would leave its peers waiting.
+        err = None
+        try:
+            for nbytes in (self.world * M * ns * esz, 256):  # gather buffer, flags
+                ptr, h = ctypes.c_void_p(), (ctypes.c_uint8 * hsz)()
+                _lib.check(lib.hx_peer_alloc(nbytes, ctypes.byref(ptr), h), "hx_peer_alloc")
+                self._mine.append(ptr.value)
+                handles.append(bytes(h))
+        except Exception as ex:  # noqa: BLE001 - re-raised after the vote
+            err = ex
+        self._vote(err, "peer buffer allocation")
         blob = torch.tensor(list(b"".join(handles)), dtype=torch.uint8, device=self.device)
         allb = torch.empty(self.world * blob.numel(), dtype=torch.uint8, device=self.device)
         dist.all_gather_into_tensor(allb, blob, group=group)
         allb = bytes(allb.cpu().numpy().tobytes())
-        self._opened = []
         bufs, flags = [], []
-        for r in range(self.world):
-            if r == self.rank:
-                bufs.append(self._mine[0])
-                flags.append(self._mine[1])
-                continue
-            ptrs = []
-            for j in range(2):
-                off = (r * 2 + j) * hsz
-                h = (ctypes.c_uint8 * hsz).from_buffer_copy(allb[off:off + hsz])
-                p = ctypes.c_void_p()
-                _lib.check(lib.hx_peer_open(h, ctypes.byref(p)), "hx_peer_open")
-                self._opened.append(p.value)
-                ptrs.append(p.value)
-            bufs.append(ptrs[0])
-            flags.append(ptrs[1])
+        try:
+            for r in range(self.world):
+                if r == self.rank:
+                    bufs.append(self._mine[0])
+                    flags.append(self._mine[1])
+                    continue
+                ptrs = []
+                for j in range(2):
+                    off = (r * 2 + j) * hsz
+                    h = (ctypes.c_uint8 * hsz).from_buffer_copy(allb[off:off + hsz])
+                    p = ctypes.c_void_p()
+                    _lib.check(lib.hx_peer_open(h, ctypes.byref(p)), "hx_peer_open")
+                    self._opened.append(p.value)
+                    ptrs.append(p.value)
+                bufs.append(ptrs[0])
+                flags.append(ptrs[1])
+        except Exception as ex:  # noqa: BLE001
+            err = ex
+        self._vote(err, "peer buffer mapping")
         self._bufs = (ctypes.c_void_p * self.world)(*bufs)
         self._flags = (ctypes.c_void_p * self.world)(*flags)
         self.epoch = 0
         self.error_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._local_view = _device_view(self._mine[0], (self.world, M, ns), dtype, self.device)
+
+    def _vote(self, err, what):
+        """All ranks agree that `what` succeeded everywhere, or all release what
+        they hold and raise."""
+        ok = torch.tensor([0 if err is not None else 1], dtype=torch.int32, device=self.device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
+        if int(ok.item()) == 1:
+            return
+        self._release()
+        raise RuntimeError(f"fused gather unavailable: {what} failed on "
+                           + (f"this rank ({err})" if err is not None else "another rank"))
+
+    def _release(self):
+        lib = _lib.load()
+        torch.cuda.synchronize(self.device)
+        for p in self._opened:
+            lib.hx_peer_close(ctypes.c_void_p(p))
+        self._opened = []
+        dist.barrier(group=self.group)  # peers unmapped before the memory goes
+        for p in self._mine:
+            lib.hx_peer_free(ctypes.c_void_p(p))
+        self._mine = []
 
     def run(self, x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Returns this rank's [world, M, ns] buffer holding all shards."""
@@ -207,16 +246,7 @@ class P2PGather:
         return self._local_view
 
     def close(self):
-        lib = _lib.load()
-        torch.cuda.synchronize(self.device)
-        for p in self._opened:
-            lib.hx_peer_close(ctypes.c_void_p(p))
-        self._opened = []
-        if self.group is not None or dist.is_initialized():
-            dist.barrier(group=self.group)  # peers unmapped before the memory goes
-        for p in self._mine:
-            lib.hx_peer_free(ctypes.c_void_p(p))
-        self._mine = []
+        self._release()
 
 
 def _device_view(ptr: int, shape, dtype, device) -> torch.Tensor:

@@ -278,8 +278,13 @@ int hx_nccl_get_unique_id(void *id_out);
 int hx_nccl_comm_init(void **comm_out, int world, const void *id, int rank);
 int hx_nccl_comm_destroy(void *comm);
 
-/* Scratch bytes a call with this descriptor needs from the caller (the
-   current kernels need none: returns 0 in *bytes). */
+/* Scratch bytes a call with this descriptor needs FROM THE CALLER: always 0.
+   Split-K plans (explicit split_k, or the planner's automatic choice) use a
+   reduction workspace that the library itself allocates with cudaMalloc on
+   first use, one per (device, stream), grown on demand and kept until exit;
+   a call made during stream capture that would need to grow it runs unsplit
+   instead.  Callers that must not allocate set split_k = 1 (or use the
+   allocation-free entry points). */
 int hx_query_workspace(const hx_gemm_desc *d, int64_t *bytes);
 
 /* Human-readable name of a status code. */

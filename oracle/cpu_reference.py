@@ -90,22 +90,45 @@ def _tinyllama(budget_s, M=1):
                 config={"workload": f"tinyllama-1.1b decode linears W8A16 M={M} (BASELINE config 4)"})
 
 
-def _lmhead(budget_s):
+_LM_CACHE = {}
+
+
+def _lm_inputs(int8, rows):
+    """Seeded LM-head operands (the GPU arm's seed and distributions), built once."""
+    key = (int8, rows)
+    if key not in _LM_CACHE:
+        g = torch.Generator().manual_seed(1238)
+        if int8:
+            a = torch.randint(-127, 128, (rows, WL.LMHEAD_K), generator=g, dtype=torch.int8)
+            w = torch.randint(-127, 128, (WL.LMHEAD_N, WL.LMHEAD_K), generator=g, dtype=torch.int8)
+        else:
+            a = torch.randn(rows, WL.LMHEAD_K, generator=g).to(torch.bfloat16)
+            w = (torch.randn(WL.LMHEAD_N, WL.LMHEAD_K, generator=g) * 0.02).to(torch.bfloat16)
+        _LM_CACHE[key] = (a, w)
+    return _LM_CACHE[key]
+
+
+def _lmhead(budget_s, int8=False):
     rows = 256
-    g = torch.Generator().manual_seed(1238)
-    a = torch.randn(rows, WL.LMHEAD_K, generator=g).to(torch.bfloat16)
-    w = (torch.randn(WL.LMHEAD_N, WL.LMHEAD_K, generator=g) * 0.02).to(torch.bfloat16)
+    a, w = _lm_inputs(int8, rows)
     with torch.no_grad():
-        t = _timeit(lambda: F.linear(a, w), 3)
+        if int8:
+            # no int8 GEMM in PyTorch-CPU: exact int32 result through fp64 (|acc| < 2^53)
+            wd = w.double()
+            t = _timeit(lambda: F.linear(a.double(), wd).to(torch.int32), 3)
+        else:
+            t = _timeit(lambda: F.linear(a, w), 3)
     flops = 2.0 * rows * WL.LMHEAD_K * WL.LMHEAD_N
     full = t * WL.LMHEAD_M / rows
-    return dict(metric="GEMM+epilogue TFLOP/s", unit="TFLOP/s", dtype="bf16",
-                value=round(flops / t / 1e12, 4), ms_per_step=round(full * 1e3, 3),
-                sample=f"PyTorch-CPU bf16 F.linear on {rows} of 16384 LM-head rows, median of 3, scaled",
-                config={"workload": "LM head 16384x2048x50304 bf16 (BASELINE config 5)"})
+    dt = "int8 (int32 acc)" if int8 else "bf16"
+    return dict(metric="GEMM+epilogue TFLOP/s", unit="TOP/s" if int8 else "TFLOP/s", dtype="int8" if int8 else "bf16",
+                value=round(flops / t / 1e12, 4), ms_per_step=round(full * 1e3, 3), scaling="strong",
+                sample=f"PyTorch-CPU {dt} F.linear on {rows} of 16384 LM-head rows, median of 3, scaled",
+                config={"workload": f"LM head 16384x2048x50304 {dt}, column-sharded (BASELINE config 5)"})
 
 
-_TABLE = {"gpt2": _gpt2, "qwen": _qwen, "tinyllama": _tinyllama, "lmhead": _lmhead}
+_TABLE = {"gpt2": _gpt2, "qwen": _qwen, "tinyllama": _tinyllama, "lmhead": _lmhead,
+          "lmhead_int8": lambda b: _lmhead(b, int8=True)}
 
 
 def time_workload(workload, budget_s=15.0, threads=1):

@@ -89,3 +89,37 @@ def test_sharded_lmhead_two_gpus():
     for r, (p, out) in enumerate(zip(procs, outs)):
         assert p.returncode == 0, f"rank {r} failed:\n{out[-3000:]}"
         assert f"rank {r} ok" in out
+
+
+DEVICE_WORKER = textwrap.dedent(r'''
+    import os, sys
+    sys.path.insert(0, os.path.join(ROOT, "hexagon-mlir_b200")); sys.path.insert(0, ROOT)
+    import numpy as np, torch
+    import qcom_hexagon_backend as q
+    from oracle import gemm_oracle as O
+    # One process, two GPUs, the same tile plans (one-CTA 198 KB-smem tiles, CTA
+    # pairs, split-K clusters): each kernel's shared-memory limit is a per-device
+    # attribute, so the second device must be configured too.
+    g = torch.Generator().manual_seed(77)
+    cases = [(1024, 768, 768, {}), (4096, 4096, 1024, {}), (256, 384, 2048, {"split_k": 2, "tile_n": 128})]
+    for M, N, K, kw in cases:
+        a = torch.randn(M, K, generator=g).half()
+        w = (torch.randn(N, K, generator=g) * 0.02).half()
+        ref = O.matmul_f32(a.float().numpy(), w.float().numpy())
+        for dev in (0, 1, 0):
+            with torch.cuda.device(dev):
+                out = q.gemm(a.to(f"cuda:{dev}"), w.to(f"cuda:{dev}"), **kw)
+                torch.cuda.synchronize(dev)
+            e = O.max_rel_err(out.float().cpu().numpy(), ref)
+            assert e <= 1e-2, (M, N, K, dev, e)
+    print("two devices ok")
+''')
+
+
+def test_one_process_two_devices():
+    """A process that drives two GPUs launches the same kernels on both."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    code = f"ROOT = {ROOT!r}\n" + DEVICE_WORKER
+    p = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=240)
+    assert p.returncode == 0 and "two devices ok" in p.stdout, (p.stdout + p.stderr)[-3000:]
