@@ -156,8 +156,8 @@ def _as_linear(gm: fx.GraphModule, n: fx.Node) -> Optional[_LinearSite]:
             return None
         x, w = n.args
         rw, rx = _rank(gm, w), _rank(gm, x)
-        if n.target in _MATMUL_FNS and (rw != 2 or rx is None or rx < 2):
-            return None  # only x[..., K] @ W[K, N]; batched products are not linears
+        if n.target in _MATMUL_FNS and (rw != 2 or (rx is not None and rx < 1)):
+            return None  # only x[..., K] @ W[K, N] with W known 2-D; batched products are not linears
         return _LinearSite(n, x, _weight_src(w), None, "kn")
     return None
 
@@ -392,8 +392,14 @@ def rewrite(gm: fx.GraphModule) -> fx.GraphModule:
                 last = graph.node_copy(cn, lambda a: mapping.get(a, a))
                 mapping[cn] = last
         tail.replace_all_uses_with(last)
-        for dead in reversed(expr):
-            graph.erase_node(dead)
+        pending = list(expr)
+        while pending:  # users before producers (the expression's nodes are not in graph order)
+            free = [d for d in pending if not d.users]
+            if not free:
+                raise RuntimeError("fused epilogue nodes still in use")
+            for d in free:
+                graph.erase_node(d)
+                pending.remove(d)
         for dead in reversed(chain):
             graph.erase_node(dead)
         graph.erase_node(n)

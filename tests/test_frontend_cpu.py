@@ -2,6 +2,7 @@
 linear(+epilogue) patterns, and the run_torch_mlir surface."""
 
 import dataclasses
+import math
 
 import pytest
 import torch
@@ -108,3 +109,141 @@ def test_workload_counts():
     assert WL.gpt2_stack_flops() == 173946175488
     assert abs(WL.qwen_stack_flops() / 1e12 - 1.387) < 1e-3
     assert abs(WL.tinyllama_decode_bytes(1) / 1e6 - 971.2) < 0.5
+
+
+# ---------------------------------------------------------------- aten / addmm / mm routes
+def _ref_linear(x, weight, bias=None, residual=None, activation=None, weight_const=False, b_layout="nk"):
+    """Torch stand-in for hx_linear with the same argument meaning (checks the
+    rewritten graph's wiring on the CPU; the kernel itself is tested on GPU)."""
+    w = weight if b_layout == "kn" else weight.t()
+    y = x @ w
+    if bias is not None:
+        y = y + bias
+    if activation == "gelu_tanh":
+        y = F.gelu(y, approximate="tanh")
+    elif activation == "silu":
+        y = F.silu(y)
+    if residual is not None:
+        y = y + residual.reshape(y.shape)
+    return y
+
+
+def _run_with_ref(gm, *args):
+    for n in gm.graph.nodes:
+        if n.op == "call_function" and n.target is FX.hx_linear:
+            n.target = _ref_linear
+    gm.recompile()
+    return gm(*args)
+
+
+class _Conv1DBlock(nn.Module):
+    """HF GPT-2's Conv1D form: addmm(bias, x2d, W[K,N]) then view, dropout, residual,
+    and the NewGELU expression written out with pow/tanh."""
+
+    def __init__(self, d=16, f=24):
+        super().__init__()
+        self.w1 = nn.Parameter(torch.randn(d, f) * 0.1)
+        self.b1 = nn.Parameter(torch.randn(f) * 0.1)
+        self.w2 = nn.Parameter(torch.randn(f, d) * 0.1)
+        self.b2 = nn.Parameter(torch.randn(d) * 0.1)
+        self.drop = nn.Dropout(0.1)
+
+    def forward(self, x):
+        h = torch.addmm(self.b1, x.view(-1, x.size(-1)), self.w1).view(x.shape[0], x.shape[1], -1)
+        h = 0.5 * h * (1.0 + torch.tanh(math.sqrt(2.0 / math.pi) * (h + 0.044715 * torch.pow(h, 3.0))))
+        y = torch.addmm(self.b2, h.view(-1, h.size(-1)), self.w2).view(x.shape)
+        return x + self.drop(y)
+
+
+def test_rewrite_addmm_newgelu_residual_export():
+    """torch.export graph (aten ops): both addmm fold their constant W[K,N] into a
+    transposed W[N,K] buffer; the GELU expression and the residual add fuse."""
+    m = _Conv1DBlock().eval()
+    x = torch.randn(2, 5, 16)
+    gm = FX.rewrite(FX.capture(m, [x], "export"))
+    calls = [n for n in gm.graph.nodes if n.op == "call_function" and n.target is FX.hx_linear]
+    assert len(calls) == 2
+    assert calls[0].kwargs.get("activation") == "gelu_tanh" and "b_layout" not in calls[0].kwargs
+    assert calls[1].kwargs.get("residual") is not None
+    tg = [str(n.target) for n in gm.graph.nodes if n.op == "call_function"]
+    assert not any("tanh" in t or "pow" in t or "addmm" in t for t in tg)
+    w0 = getattr(gm, calls[0].args[1].target)
+    assert torch.equal(w0, m.w1.detach().t())
+    torch.testing.assert_close(_run_with_ref(gm, x), m(x), rtol=1e-5, atol=1e-5)
+
+
+def test_rewrite_addmm_symbolic_trace():
+    m = _Conv1DBlock().eval()
+    x = torch.randn(2, 5, 16)
+    gm = FX.rewrite(FX.capture(m, [x], "trace"))
+    assert FX.count_hx_calls(gm) == 2
+    torch.testing.assert_close(_run_with_ref(gm, x), m(x), rtol=1e-5, atol=1e-5)
+
+
+class _MatmulForms(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.a = nn.Parameter(torch.randn(16, 8))
+        self.b = nn.Parameter(torch.randn(8, 12))
+
+    def forward(self, x, wdyn):
+        y = torch.mm(x, self.a)                 # constant B[K,N]
+        y = F.silu(y @ self.b)                  # operator.matmul + SiLU
+        z = torch.matmul(y, wdyn)               # a non-constant B[K,N]: runs as kn
+        return z + x[:, :4]
+
+
+@pytest.mark.parametrize("mode", ["trace", "export"])
+def test_rewrite_mm_matmul_forms(mode):
+    m = _MatmulForms()
+    x, wd = torch.randn(6, 16), torch.randn(12, 4)
+    gm = FX.rewrite(FX.capture(m, [x, wd], mode))
+    calls = [n for n in gm.graph.nodes if n.op == "call_function" and n.target is FX.hx_linear]
+    # a symbolic trace has no shape for the input `wdyn`, so that product stays a torch op
+    assert len(calls) == (3 if mode == "export" else 2)
+    assert calls[1].kwargs.get("activation") == "silu"
+    if mode == "export":
+        assert calls[2].kwargs.get("b_layout") == "kn" and calls[2].kwargs.get("residual") is not None
+    torch.testing.assert_close(_run_with_ref(gm, x, wd), m(x, wd), rtol=1e-5, atol=1e-5)
+
+
+def test_batched_matmul_is_not_a_linear():
+    class B(nn.Module):
+        def forward(self, q, k):
+            return torch.matmul(q, k.transpose(-1, -2))
+
+    q = torch.randn(2, 3, 5, 4)
+    gm = FX.rewrite(FX.capture(B(), [q, q], "export"))
+    assert FX.count_hx_calls(gm) == 0
+
+
+def test_training_dropout_blocks_fusion():
+    class D(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.l = nn.Linear(8, 8)
+
+        def forward(self, x):
+            return x + F.dropout(self.l(x), 0.5)  # training=True by default: not transparent
+
+    gm = FX.rewrite(fx.symbolic_trace(D()))
+    node = [n for n in gm.graph.nodes if n.target is FX.hx_linear][0]
+    assert "residual" not in node.kwargs
+
+
+def test_hf_gpt2_lmhead_routes_every_linear():
+    """Random-init HF GPT2LMHeadModel (GPT2Config(), 12 layers, fp16) through the
+    export capture: every Conv1D addmm (4 per layer) and the LM head become
+    fused kernel calls, with GELU and both residual adds in the epilogue."""
+    transformers = pytest.importorskip("transformers")
+    cfg = transformers.GPT2Config()
+    cfg.use_cache = False
+    torch.manual_seed(0)
+    m = transformers.GPT2LMHeadModel(cfg).eval().half()
+    ids = torch.randint(0, cfg.vocab_size, (1, 8))
+    gm = FX.rewrite(FX.capture(m, [ids], "auto"))
+    calls = [n for n in gm.graph.nodes if n.op == "call_function" and n.target is FX.hx_linear]
+    assert len(calls) == 12 * 4 + 1
+    assert sum(n.kwargs.get("activation") == "gelu_tanh" for n in calls) == 12
+    assert sum(n.kwargs.get("residual") is not None for n in calls) == 24
+    assert not any("addmm" in str(n.target) for n in gm.graph.nodes)
