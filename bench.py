@@ -7,8 +7,10 @@ Default workload, at every N (the configuration the headline metric is
 quoted on at 1/2/4/8 GPUs): the LM-head GEMM, bf16, M=16384 tokens x
 K=2048 x N=50304, weights N(0,0.02), activations N(0,1), column-sharded
 over the N ranks.  A "step" is one pass of the sharded GEMM; at N > 1 it
-includes the all-gather of the logits onto every rank (by default fused
-into the GEMM's epilogue as stores over NVLink).  value = 2*M*N*K / step
+includes the all-gather of the logits onto every rank (by default the GEMM
+runs in row chunks and each finished chunk is DMA-copied over NVLink into
+every peer's buffer while the next chunk computes; --gather p2p fuses the
+transfer into the GEMM's epilogue stores instead, --gather nccl uses NCCL).  value = 2*M*N*K / step
 time (max over ranks), strong scaling.  The inputs (1.9 GB) exceed the
 126 MB L2, so no flush is needed between steps.
 
@@ -381,10 +383,12 @@ def run_tinyllama(args, world, rank, dev, peaks, peak_src):
 def run_lmhead(args, world, rank, dev, peaks, peak_src):
     """Config 5: LM head M=16384 x K=2048 x N=50304, bf16 (or int8 W8A8 with int32
     accumulate, --lm-dtype int8), column-sharded over the ranks.  At N > 1 every step
-    also all-gathers the logits into [world, M, N/world] on every rank: by default the
-    GEMM's own epilogue stores each output chunk into every peer's buffer over NVLink
-    (one fused launch, hx_sharded_gemm_gather_p2p); --gather nccl runs the GEMM in M
-    chunks with chunk c's NCCL all-gather on a side stream overlapping chunk c+1.
+    also all-gathers the logits into [world, M, N/world] on every rank: by default
+    (--gather ce) the GEMM runs in row chunks and each finished chunk is copied by the
+    copy engines into every peer's buffer (hx_sharded_gemm_gather_ce); --gather p2p is
+    one fused launch whose epilogue stores into the peers (hx_sharded_gemm_gather_p2p);
+    --gather nccl runs the GEMM in M chunks with chunk c's NCCL all-gather on a side
+    stream overlapping chunk c+1.
     gemm_only reports the sharded GEMM alone."""
     from qcom_hexagon_backend import ops
     from qcom_hexagon_backend.sharding import shard_range, shard_width
@@ -409,7 +413,8 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
     odt = torch.int32 if int8 else torch.bfloat16
     esz = 4 if int8 else 2
     out = torch.empty(M, ns, dtype=odt, device=dev)
-    p2p = world > 1 and args.gather == "p2p"
+    p2p = world > 1 and args.gather in ("p2p", "ce")
+    transfer = "copy_engine" if args.gather == "ce" else "epilogue"
     main = torch.cuda.current_stream(dev)
 
     def gemm_only():
@@ -419,7 +424,7 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
     if p2p:
         from qcom_hexagon_backend.sharding import P2PGather
         try:  # all ranks construct it or all raise (collective vote inside)
-            pg = P2PGather(M, ns, odt)
+            pg = P2PGather(M, ns, odt, transfer=transfer, chunks=args.ce_chunks)
         except RuntimeError as ex:
             if rank == 0:
                 print(f"{ex}; using NCCL", file=sys.stderr)
@@ -534,7 +539,8 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
                 "unit": "GB/s" if t_link >= t_tensor else unit,
                 "frac": round(target / ms, 4), "traffic": traffic if p2p else None,
                 "target_ms": round(target, 4), "tensor_ms": round(t_tensor, 4), "nvlink_ms": round(t_link, 4),
-                "kernel": "hx_gemm_sm100_2sm_kernel (fused peer-store epilogue)" if p2p
+                "kernel": ("hx_gemm_sm100_2sm_kernel (fused peer-store epilogue)" if transfer == "epilogue"
+                           else "hx_gemm_sm100_2sm_kernel + copy-engine peer copies") if p2p
                 else "hx_gemm_sm100_2sm_kernel + NCCL all-gather",
                 "peak_source": f"{peak_src} {peak_key} and measured 770 GB/s NVLink peer copy per direction"}
     line = {"metric": "GEMM+epilogue TFLOP/s", "value": round(tflops, 2), "unit": unit, "n_gpus": world,
@@ -545,7 +551,10 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
                        "M": M, "K": K, "N": N, "shard_cols": ns,
                        "parallelism": f"tp{world} (N-sharded"
                        + ((", logits all-gathered into [world, M, N/world] by the GEMM's own epilogue "
-                           "stores over NVLink (fused, hx_sharded_gemm_gather_p2p))" if p2p else
+                           "stores over NVLink (fused, hx_sharded_gemm_gather_p2p))" if p2p and transfer == "epilogue" else
+                           ", logits all-gathered into [world, M, N/world]: GEMM in row chunks, each chunk "
+                           "DMA-copied to every peer over NVLink while the next computes (hx_sharded_gemm_gather_ce))"
+                           if p2p else
                            ", logits all-gathered over NCCL into [world, M, N/world], overlapped in "
                            f"{chunks} M-chunks)") if world > 1 else ")"),
                        "l2": "inputs (1.9 GB/step at N=1) larger than L2; no flush"},
@@ -553,9 +562,9 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
                           "ms_per_step": round(gemm_ms, 4)},
             "e2e": {"value": round(e2e_value, 2), "unit": unit, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                    "api": ("sharding.P2PGather.run" if p2p else "ops.gemm" + (" + NCCL all-gather" if world > 1 else ""))
+                    "api": (f"sharding.P2PGather(transfer={transfer!r}).run" if p2p else "ops.gemm" + (" + NCCL all-gather" if world > 1 else ""))
                     + " with A copied from pinned host memory and this rank's logits shard copied back"},
-            "gpu_launches": args.steps * (3 if p2p else chunks),
+            "gpu_launches": args.steps * ((3 if transfer == "epilogue" else 2 + pg.last_chunks) if p2p else chunks),
             "roofline": roof,
             "clocks": clocks}
     if world > 1:
@@ -613,8 +622,10 @@ def main(argv=None):
     ap.add_argument("--layers", type=int, default=22, help="decoder layers for --workload tinyllama")
     ap.add_argument("--chain", action="store_true",
                     help="stacks: run consecutive linears as one persistent launch (chain_gemms)")
-    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
-                    help="LM head at N>1: fused GEMM + NVLink all-gather (p2p) or GEMM + NCCL")
+    ap.add_argument("--gather", choices=["p2p", "ce", "nccl"], default="ce",
+                    help="LM head at N>1: all-gather by the GEMM's epilogue stores over NVLink (p2p), "
+                         "by copy-engine DMA of finished row chunks (ce), or by NCCL")
+    ap.add_argument("--ce-chunks", type=int, default=0, help="row chunks of --gather ce (0 = automatic)")
     ap.add_argument("--lm-dtype", choices=["bf16", "int8"], default="bf16",
                     help="LM head: bf16, or the int8 W8A8 variant (int32 accumulate)")
     ap.add_argument("--lm-rows", type=int, default=0,

@@ -1345,6 +1345,129 @@ int hx_sharded_gemm_gather_p2p(const hx_gemm_desc *d, int rank, int world, void 
   return hx::peer_barrier(flags, rank, world, 2 * epoch + 2, error_flag, s);
 }
 
+// Per-device streams and events of the copy-engine gather: one stream per
+// peer slot (copies to different peers run on different DMA engines at once)
+// and a pool of events for the chunk hand-offs.  Created on first use, kept
+// until exit.
+namespace hx {
+namespace {
+constexpr int kCeMaxChunks = 16;
+struct CeResources {
+  bool ready = false;
+  cudaStream_t peer_stream[7];
+  cudaEvent_t chunk_done[kCeMaxChunks];
+  cudaEvent_t entry_done, peer_done[7];
+};
+CeResources g_ce[kMaxDevices];
+std::mutex g_ce_mu;
+
+int ce_resources(CeResources **out) {
+  const int dev = current_device_ordinal();
+  if (dev < 0) return arg_fail("device index out of range");
+  std::lock_guard<std::mutex> lock(g_ce_mu);
+  CeResources &r = g_ce[dev];
+  if (!r.ready) {
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < 7 && e == cudaSuccess; ++i)
+      e = cudaStreamCreateWithFlags(&r.peer_stream[i], cudaStreamNonBlocking);
+    for (int i = 0; i < kCeMaxChunks && e == cudaSuccess; ++i)
+      e = cudaEventCreateWithFlags(&r.chunk_done[i], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&r.entry_done, cudaEventDisableTiming);
+    for (int i = 0; i < 7 && e == cudaSuccess; ++i)
+      e = cudaEventCreateWithFlags(&r.peer_done[i], cudaEventDisableTiming);
+    if (e != cudaSuccess) return cuda_fail(e, "copy-engine gather set-up");
+    r.ready = true;
+  }
+  *out = &r;
+  return HX_OK;
+}
+}  // namespace
+}  // namespace hx
+
+int hx_sharded_gemm_gather_ce(const hx_gemm_desc *d, int rank, int world, void *const *gathered,
+                              int32_t *const *flags, int32_t epoch, int32_t *error_flag, int chunks,
+                              void *stream) {
+  hx::g_last_error.clear();
+  if (!d || !gathered || !flags || world < 1 || world > 8 || rank < 0 || rank >= world || epoch < 0 ||
+      epoch > (INT32_MAX - 2) / 2 || chunks < 0 || chunks > hx::kCeMaxChunks)
+    return HX_E_INVALID_ARG;
+  for (int r = 0; r < world; ++r)
+    if (!gathered[r] || !flags[r]) return HX_E_INVALID_ARG;
+  if (d->ldc != d->N) {
+    hx::g_last_error = "gather needs a contiguous shard (ldc == N)";
+    return HX_E_INVALID_ARG;
+  }
+  const int cz = hx::esize(d->c_dtype), az = hx::esize(d->a_dtype);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t slot = static_cast<size_t>(rank) * d->M * d->N * cz;
+  hx_gemm_desc dd = *d;
+  dd.C = static_cast<uint8_t *>(gathered[rank]) + slot;
+  if (world == 1) return hx::gemm_impl(&dd, s);
+  hx::CeResources *R = nullptr;
+  int rc = hx::ce_resources(&R);
+  if (rc != HX_OK) return rc;
+  // Row chunks: whole 256-row pair tiles.  Automatic: up to 6, measured best
+  // at the 16384-row LM head on 2 GPUs (fewer leave a long last copy, more
+  // add per-chunk GEMM tails).
+  if (chunks == 0) chunks = static_cast<int>(std::min<int64_t>(6, std::max<int64_t>(1, d->M / 2048)));
+  int64_t rows = (d->M + chunks - 1) / chunks;
+  rows = std::max<int64_t>(256, (rows + 255) / 256 * 256);
+  chunks = static_cast<int>((d->M + rows - 1) / rows);
+  cudaError_t e;
+  // Entry barrier on the first peer stream, concurrent with the first GEMM
+  // chunk (which writes only this rank's own buffer): every peer has reached
+  // this call, so its buffer may be overwritten.
+  e = cudaEventRecord(R->chunk_done[0], s);  // peer streams start after the caller's prior work
+  if (e != cudaSuccess) return hx::cuda_fail(e, "cudaEventRecord");
+  e = cudaStreamWaitEvent(R->peer_stream[0], R->chunk_done[0], 0);
+  if (e != cudaSuccess) return hx::cuda_fail(e, "cudaStreamWaitEvent");
+  rc = hx::peer_barrier(flags, rank, world, 2 * epoch + 1, error_flag, R->peer_stream[0]);
+  if (rc != HX_OK) return rc;
+  if ((e = cudaEventRecord(R->entry_done, R->peer_stream[0])) != cudaSuccess)
+    return hx::cuda_fail(e, "cudaEventRecord");
+  const int npeer = world - 1;
+  for (int i = 1; i < npeer; ++i)
+    if ((e = cudaStreamWaitEvent(R->peer_stream[i], R->entry_done, 0)) != cudaSuccess)
+      return hx::cuda_fail(e, "cudaStreamWaitEvent");
+  for (int c = 0; c < chunks; ++c) {
+    const int64_t r0 = c * rows, nr = std::min<int64_t>(rows, d->M - r0);
+    hx_gemm_desc cd = dd;
+    cd.M = nr;
+    cd.A = static_cast<const uint8_t *>(d->A) + static_cast<size_t>(r0) * d->lda * az;
+    cd.C = static_cast<uint8_t *>(dd.C) + static_cast<size_t>(r0) * d->N * cz;
+    if (cd.residual)
+      cd.residual = static_cast<const uint8_t *>(d->residual) + static_cast<size_t>(r0) * d->ldr * cz;
+    rc = hx::gemm_impl(&cd, s);
+    if (rc != HX_OK) return rc;
+    if ((e = cudaEventRecord(R->chunk_done[c], s)) != cudaSuccess) return hx::cuda_fail(e, "cudaEventRecord");
+    const size_t bytes = static_cast<size_t>(nr) * d->N * cz;
+    for (int i = 0, r = 0; r < world; ++r) {
+      if (r == rank) continue;
+      cudaStream_t ps = R->peer_stream[i++];
+      if ((e = cudaStreamWaitEvent(ps, R->chunk_done[c], 0)) != cudaSuccess)
+        return hx::cuda_fail(e, "cudaStreamWaitEvent");
+      e = cudaMemcpyAsync(static_cast<uint8_t *>(gathered[r]) + slot + static_cast<size_t>(r0) * d->N * cz,
+                          cd.C, bytes, cudaMemcpyDeviceToDevice, ps);
+      if (e != cudaSuccess) return hx::cuda_fail(e, "cudaMemcpyAsync(peer chunk)");
+    }
+  }
+  // Exit: after every copy of this rank has landed, publish and wait for the
+  // peers' copies into this rank's buffer (bounded).
+  for (int i = 1; i < npeer; ++i) {
+    if ((e = cudaEventRecord(R->peer_done[i], R->peer_stream[i])) != cudaSuccess)
+      return hx::cuda_fail(e, "cudaEventRecord");
+    if ((e = cudaStreamWaitEvent(R->peer_stream[0], R->peer_done[i], 0)) != cudaSuccess)
+      return hx::cuda_fail(e, "cudaStreamWaitEvent");
+  }
+  rc = hx::peer_barrier(flags, rank, world, 2 * epoch + 2, error_flag, R->peer_stream[0]);
+  if (rc != HX_OK) return rc;
+  if ((e = cudaEventRecord(R->peer_done[0], R->peer_stream[0])) != cudaSuccess)
+    return hx::cuda_fail(e, "cudaEventRecord");
+  if ((e = cudaStreamWaitEvent(s, R->peer_done[0], 0)) != cudaSuccess)
+    return hx::cuda_fail(e, "cudaStreamWaitEvent");
+  return HX_OK;
+}
+
 int hx_sharded_gemm_allgather(const hx_gemm_desc *d, int rank, int world, void *comm,
                               void *gathered, void *stream) {
   if (!d || world < 1 || rank < 0 || rank >= world) return HX_E_INVALID_ARG;

@@ -137,8 +137,23 @@ class ColumnShardedLinear:
         return rows_from_shards(gathered, self.N)
 
 
+def ce_chunk_count(M: int, chunks: int = 0) -> int:
+    """Row chunks hx_sharded_gemm_gather_ce runs for M rows and a requested count."""
+    if chunks == 0:
+        chunks = min(6, max(1, M // 2048))
+    rows = -(-M // chunks)
+    rows = max(256, -(-rows // 256) * 256)
+    return -(-M // rows)
+
+
 class P2PGather:
-    """Fused sharded GEMM + all-gather over NVLink (hx_sharded_gemm_gather_p2p).
+    """Sharded GEMM + all-gather over NVLink into peer-mapped buffers.
+
+    transfer="epilogue": one fused launch (hx_sharded_gemm_gather_p2p) whose
+    GEMM epilogue stores each output chunk into every rank's buffer;
+    transfer="copy_engine": the GEMM in row chunks with each finished chunk
+    copied to the peers by DMA (hx_sharded_gemm_gather_ce), overlapping the
+    next chunk.
 
     Every rank owns a [world, M, ns] gather buffer and a flag array in its own
     GPU memory; the buffers are exported as CUDA IPC handles, exchanged with
@@ -154,7 +169,11 @@ class P2PGather:
     The caller should treat the gather as failed on all ranks.
     """
 
-    def __init__(self, M: int, ns: int, dtype: torch.dtype, group=None):
+    def __init__(self, M: int, ns: int, dtype: torch.dtype, group=None, transfer: str = "epilogue",
+                 chunks: int = 0):
+        if transfer not in ("epilogue", "copy_engine"):
+            raise ValueError("transfer must be 'epilogue' or 'copy_engine'")
+        self.transfer, self.chunks = transfer, chunks
         lib = _lib.load()
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         if self.world > 8:
@@ -209,6 +228,12 @@ class P2PGather:
         self.error_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._local_view = _device_view(self._mine[0], (self.world, M, ns), dtype, self.device)
 
+    @property
+    def last_chunks(self) -> int:
+        """GEMM launches per run() of the copy-engine transfer (the library's
+        chunking rule: whole 256-row tiles, up to 6 automatic chunks)."""
+        return ce_chunk_count(self.M, self.chunks)
+
     def _vote(self, err, what):
         """All ranks agree that `what` succeeded everywhere, or all release what
         they hold and raise."""
@@ -237,11 +262,17 @@ class P2PGather:
                                   epilogue="bias" if bias is not None else "none", b_const=True)
         lib = _lib.load()
         with torch.cuda.device(dev):
-            rc = lib.hx_sharded_gemm_gather_p2p(ctypes.byref(d), self.rank, self.world, self._bufs,
-                                                self._flags, self.epoch,
-                                                ctypes.c_void_p(self.error_flag.data_ptr()),
-                                                ctypes.c_void_p(ops._stream_ptr(dev)))
-        _lib.check(rc, "hx_sharded_gemm_gather_p2p")
+            if self.transfer == "epilogue":
+                rc = lib.hx_sharded_gemm_gather_p2p(ctypes.byref(d), self.rank, self.world, self._bufs,
+                                                    self._flags, self.epoch,
+                                                    ctypes.c_void_p(self.error_flag.data_ptr()),
+                                                    ctypes.c_void_p(ops._stream_ptr(dev)))
+            else:
+                rc = lib.hx_sharded_gemm_gather_ce(ctypes.byref(d), self.rank, self.world, self._bufs,
+                                                   self._flags, self.epoch,
+                                                   ctypes.c_void_p(self.error_flag.data_ptr()), self.chunks,
+                                                   ctypes.c_void_p(ops._stream_ptr(dev)))
+        _lib.check(rc, "hx_sharded_gemm_gather_" + ("p2p" if self.transfer == "epilogue" else "ce"))
         self.epoch += 1
         return self._local_view
 

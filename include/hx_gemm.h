@@ -255,6 +255,18 @@ int hx_sharded_gemm_gather_p2p(const hx_gemm_desc *d, int rank, int world, void 
                                int32_t *const *flags, int32_t epoch, int32_t *error_flag,
                                void *stream);
 
+/* The same result as hx_sharded_gemm_gather_p2p, with the transfer on the
+   copy engines instead of the GEMM's epilogue: the GEMM runs in `chunks` row
+   chunks (0 = automatic: min(6, M/2048); at most 16) on `stream` with every SM, and as each
+   chunk completes it is copied (cudaMemcpyAsync, peer-mapped destination)
+   into every peer's buffer, one library-owned stream per peer, overlapping
+   the next chunk's GEMM.  Entry and exit are the same bounded flag barriers
+   (error 41 on timeout); the call returns with `stream` ordered after the
+   exit barrier.  Reference: none (no multi-device path in the reference). */
+int hx_sharded_gemm_gather_ce(const hx_gemm_desc *d, int rank, int world, void *const *gathered,
+                              int32_t *const *flags, int32_t epoch, int32_t *error_flag, int chunks,
+                              void *stream);
+
 /* Device memory other processes' GPUs can map: cudaMalloc'ed and zeroed on the
    current device, exported as a CUDA IPC handle of hx_peer_handle_size()
    bytes.  hx_peer_open maps a peer's handle into this process (peer access

@@ -155,7 +155,7 @@ def test_config5_shard_widths(cuda_device, world, kind):
 
 
 # ---------------------------------------------------------------- fused gather, one GPU
-def _p2p_call(q, a, w, bufs, flags, world, rank, epoch, err, odt=torch.bfloat16):
+def _p2p_call(q, a, w, bufs, flags, world, rank, epoch, err, odt=torch.bfloat16, ce_chunks=None):
     from qcom_hexagon_backend import _lib, ops
 
     lib = _lib.load()
@@ -165,14 +165,19 @@ def _p2p_call(q, a, w, bufs, flags, world, rank, epoch, err, odt=torch.bfloat16)
     cb = (ctypes.c_void_p * world)(*[b.data_ptr() for b in bufs])
     cf = (ctypes.c_void_p * world)(*[f.data_ptr() for f in flags])
     with torch.cuda.device(dev):
+        if ce_chunks is not None:
+            return lib.hx_sharded_gemm_gather_ce(ctypes.byref(d), rank, world, cb, cf, epoch,
+                                                 ctypes.c_void_p(err.data_ptr()), ce_chunks,
+                                                 ctypes.c_void_p(ops._stream_ptr(dev)))
         return lib.hx_sharded_gemm_gather_p2p(ctypes.byref(d), rank, world, cb, cf, epoch,
                                               ctypes.c_void_p(err.data_ptr()),
                                               ctypes.c_void_p(ops._stream_ptr(dev)))
 
 
+@pytest.mark.parametrize("transfer", ["epilogue", "ce_auto", "ce_3"])
 @pytest.mark.parametrize("world,rank", [(2, 0), (2, 1), (4, 2), (8, 5)])
 @pytest.mark.parametrize("kind", ["bf16", "int8"])
-def test_peer_store_epilogue_one_gpu(cuda_device, world, rank, kind):
+def test_peer_store_epilogue_one_gpu(cuda_device, world, rank, kind, transfer):
     """The GEMM's epilogue stores this rank's shard into every rank's gather
     buffer.  All `world` buffers live on this GPU; the other ranks' flags are
     pre-published (value 1000 >= every barrier value used here), so both
@@ -197,7 +202,8 @@ def test_peer_store_epilogue_one_gpu(cuda_device, world, rank, kind):
     err = torch.zeros(1, dtype=torch.int32, device=d)
     for epoch in range(3):
         ad = (a.to(d) if kind == "int8" else (a.float() * (epoch + 1)).to(torch.bfloat16).to(d))
-        rc = _p2p_call(q, ad, w.to(d), bufs, flags, world, rank, epoch, err, odt)
+        ce = None if transfer == "epilogue" else (0 if transfer == "ce_auto" else 3)
+        rc = _p2p_call(q, ad, w.to(d), bufs, flags, world, rank, epoch, err, odt, ce)
         assert rc == 0, _lib.load().hx_last_error()
         torch.cuda.synchronize()
         assert int(err.item()) == 0

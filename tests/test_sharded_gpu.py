@@ -54,6 +54,17 @@ WORKER = textwrap.dedent(r'''
         e4 = O.max_rel_err(y4, ref * (it + 1))
         assert y4.shape == (M, N) and e4 <= 1e-2, (it, e4)
     pg.close()
+    # (d) the same through the copy engines, GEMM in row chunks
+    for chunks in (0, 3):
+        pg = S.P2PGather(M, lin.ns, torch.bfloat16, transfer="copy_engine", chunks=chunks)
+        for it in range(3):
+            buf = pg.run(a.cuda() * (it + 1), lin.weight)
+            torch.cuda.synchronize()
+            assert int(pg.error_flag.item()) == 0, int(pg.error_flag.item())
+            y5 = S.rows_from_shards(buf, N).float().cpu().numpy()
+            e5 = O.max_rel_err(y5, ref * (it + 1))
+            assert y5.shape == (M, N) and e5 <= 1e-2, (chunks, it, e5)
+        pg.close()
     torch.cuda.synchronize(); comm.close(); dist.destroy_process_group()
     print("rank", rank, "ok", e1, e2, e3, e4)
 ''')
@@ -67,10 +78,10 @@ def _port():
     return p
 
 
-def test_sharded_lmhead_two_gpus():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    world = 2
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_lmhead_multi_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     port = _port()
     env = dict(os.environ, MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world),
                NCCL_NVLS_ENABLE="0")
