@@ -74,6 +74,12 @@ struct GemmParams {
   uint4 *ws;                      // split-K: [tile][rank][BN/32][8][128] x 16 B of partials
   int32_t red_smem;               // split-K: fetch remote partials into the ring (else read L2)
   int32_t b_const;                // B is constant: fetch the first B tiles before the dependency wait
+  // Batched GEMM (batch > 1): tile t belongs to item t / batch_tiles; A and B
+  // are 3-D tensor maps (item as the outer dimension, 2-D K-block loads) and
+  // C / residual rows are flattened, item b's row r at b * batch_rows + r.
+  int32_t batch;                  // items (1 = a plain GEMM)
+  int32_t batch_tiles;            // m_tiles * n_tiles of one item
+  int32_t batch_rows;             // rows of one item (a multiple of kBM)
   EpiArgs epi;
 };
 
@@ -110,6 +116,16 @@ __device__ __forceinline__ void tile_coords(int t, const GemmParams &p, int &m_b
   const int r = t - g * per_group;
   m_blk = first_m + r % gsize;
   n_blk = r / gsize;
+}
+
+// Tile t of a (possibly batched) launch: item b and its m / n blocks.
+__device__ __forceinline__ void tile_coords_b(int t, const GemmParams &p, int &b, int &m_blk, int &n_blk) {
+  b = 0;
+  if (p.batch > 1) {
+    b = t / p.batch_tiles;
+    t -= b * p.batch_tiles;
+  }
+  tile_coords(t, p, m_blk, n_blk);
 }
 
 __device__ __forceinline__ uint32_t gemm_cluster_rank() {
@@ -358,21 +374,29 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    auto load_a = [&](uint64_t *fb, int stage, int m0, int sb) {
+    auto load_a = [&](uint64_t *fb, int stage, int m0, int sb, int b) {
       uint8_t *dstA = sA + stage * A_ST;
-      if (!B_MN && p.use3d)
+      if (p.batch > 1)
+        tma_load_3d(dstA, &tmA, fb, sb * Cfg::kBKElems, m0, b);
+      else if (!B_MN && p.use3d)
         tma_load_3d(dstA, &tmA, fb, 0, m0, sb * p.kbs);
       else
         tma_load_2d(dstA, &tmA, fb, sb * Cfg::kBKElems, m0);
     };
-    auto load_b = [&](uint64_t *fb, int stage, int n_blk, int sb) {
+    auto load_b = [&](uint64_t *fb, int stage, int n_blk, int sb, int b) {
       uint8_t *dstB = sB + stage * B_ST;
-      if constexpr (B_MN) {  // kbs == 1, 2-D maps
+      if constexpr (B_MN) {  // kbs == 1, 2-D maps (3-D with the batch item outermost)
         const int kx = sb * Cfg::kBKElems;
         const int n0 = n_blk * BN;
 #pragma unroll
-        for (int j = 0; j < BN / Cfg::kMNChunk; ++j)
-          tma_load_2d(dstB + j * (Cfg::kBKElems * 128), &tmB, fb, n0 + j * Cfg::kMNChunk, kx);
+        for (int j = 0; j < BN / Cfg::kMNChunk; ++j) {
+          if (p.batch > 1)
+            tma_load_3d(dstB + j * (Cfg::kBKElems * 128), &tmB, fb, n0 + j * Cfg::kMNChunk, kx, b);
+          else
+            tma_load_2d(dstB + j * (Cfg::kBKElems * 128), &tmB, fb, n0 + j * Cfg::kMNChunk, kx);
+        }
+      } else if (p.batch > 1) {  // kbs == 1, no SWIGLU
+        tma_load_3d(dstB, &tmB, fb, sb * Cfg::kBKElems, n_blk * BN, b);
       } else if (p.use3d) {
         const int kz = sb * p.kbs;
         if constexpr (SWIGLU) {
@@ -398,11 +422,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     int pre = 0;
     if (p.b_const && t_first < p.total_tiles) pre = min(STAGES, sb_end - sb_begin);
     if (lane == 0 && pre > 0) {
-      int m_blk, n_blk;
-      tile_coords(t_first, p, m_blk, n_blk);
+      int b, m_blk, n_blk;
+      tile_coords_b(t_first, p, b, m_blk, n_blk);
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&full_bar[i], A_ST + B_ST);
-        load_b(&full_bar[i], i, n_blk, sb_begin + i);
+        load_b(&full_bar[i], i, n_blk, sb_begin + i, b);
       }
     }
     grid_dep_wait();
@@ -412,8 +436,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int64_t issued = pre;
     bool ok = true;
     for (int t = t_first; t < p.total_tiles && ok; t += t_step) {
-      int m_blk, n_blk;
-      tile_coords(t, p, m_blk, n_blk);
+      int b, m_blk, n_blk;
+      tile_coords_b(t, p, b, m_blk, n_blk);
       const int m0 = m_blk * kBM;
       for (int sb = sb_begin; sb < sb_end; ++sb) {
         const bool early = (t == t_first) && (sb - sb_begin < pre);  // B already in flight
@@ -430,8 +454,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           uint64_t *fb = &full_bar[stage];
           if (!early) mbar_arrive_expect_tx(fb, A_ST + B_ST);
-          load_a(fb, stage, m0, sb);
-          if (!early) load_b(fb, stage, n_blk, sb);
+          load_a(fb, stage, m0, sb, b);
+          if (!early) load_b(fb, stage, n_blk, sb, b);
         }
         __syncwarp();
         if (!early) ++issued;
@@ -541,11 +565,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_in_tile = q * 32 + lane;
     int it = 0;
     for (int t = t_first; t < p.total_tiles; t += t_step, ++it) {
-      int m_blk, n_blk;
-      tile_coords(t, p, m_blk, n_blk);
+      int b, m_blk, n_blk;
+      tile_coords_b(t, p, b, m_blk, n_blk);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      const int m = m_blk * kBM + row_in_tile;
+      const int m = b * p.batch_rows + m_blk * kBM + row_in_tile;  // flattened row of C
       const int c0 = (warp - 2) / 4;
       Pre16 pf;
       if (S == 1) epi_row_prefetch<SWIGLU>(p.epi, m, n_blk * Cfg::kBNOut + c0 * 32, pf);

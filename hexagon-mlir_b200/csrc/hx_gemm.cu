@@ -143,6 +143,37 @@ int make_tmap3(CUtensorMap *map, const void *ptr, int dtype, uint64_t inner, uin
   return HX_OK;
 }
 
+// 3-D view for batched GEMMs: x = inner (contiguous), y = rows, z = batch
+// item; byte strides of a row and of an item; box {box_x, box_y, 1}.
+int make_tmap_batched(CUtensorMap *map, const void *ptr, int dtype, uint64_t inner, uint64_t rows,
+                      uint64_t items, uint64_t row_stride_bytes, uint64_t item_stride_bytes,
+                      uint32_t box_x, uint32_t box_y) {
+  auto enc = get_encode();
+  if (!enc) {
+    g_last_error = "cuTensorMapEncodeTiled unavailable";
+    return HX_E_CUDA;
+  }
+  CUtensorMapDataType dt;
+  switch (dtype) {
+    case HX_F16: dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16; break;
+    case HX_BF16: dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; break;
+    case HX_S8: dt = CU_TENSOR_MAP_DATA_TYPE_UINT8; break;
+    default: return unsupported("tensor map dtype");
+  }
+  cuuint64_t dims[3] = {inner, rows, items};
+  cuuint64_t strides[2] = {row_stride_bytes, item_stride_bytes};
+  cuuint32_t box[3] = {box_x, box_y, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, dt, 3, const_cast<void *>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    g_last_error = "cuTensorMapEncodeTiled (batched) failed (code " + std::to_string(int(r)) + ")";
+    return HX_E_UNSUPPORTED;
+  }
+  return HX_OK;
+}
+
 int esize(int dtype) {
   switch (dtype) {
     case HX_F16:
@@ -398,7 +429,14 @@ struct PeerTargets {
   void *C[7];
 };
 
-int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = nullptr) {
+// Batch items of hx_gemm_batched: count and element strides between items.
+struct BatchSpec {
+  int64_t count, sa, sb, sc, sr;
+};
+constexpr int kNeedsLoop = 2;  // internal: the batch is not one launch; run item by item
+
+int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = nullptr,
+              const BatchSpec *bt = nullptr) {
   int rc = validate(d);
   if (rc != HX_OK) return rc;
   if (d->M == 0 || d->N == 0) return HX_OK;
@@ -414,6 +452,17 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = 
   const bool bmn = d->b_layout == HX_B_KN;
   const bool tma_ok = !d->force_simt && d->K > 0 && aligned16(d->A) && aligned16(d->B) &&
                       (d->lda * ez) % 16 == 0 && (d->ldb * ez) % 16 == 0;
+  // One launch over every batch item when each item's rows are whole tiles
+  // and C (and the residual) are items of rows back to back.
+  const bool batched = bt != nullptr && bt->count > 1;
+  if (batched) {
+    const bool one_launch = tma_ok && !swiglu && peers == nullptr && d->M % kBM == 0 &&
+                            bt->sc == d->M * d->ldc && (!d->residual || bt->sr == d->M * d->ldr) &&
+                            (bt->sa * ez) % 16 == 0 && (bt->sb * ez) % 16 == 0 && d->split_k <= 1 &&
+                            bt->sa >= d->M * d->lda && bt->sb >= (bmn ? d->K : d->N) * d->ldb &&
+                            bt->count * d->M <= INT32_MAX && bt->count <= 65535;
+    if (!one_launch) return kNeedsLoop;
+  }
   if (!tma_ok) return run_simt(d, s);
 
   if (d->split_k < 0 || d->split_k > 8) return arg_fail("split_k must be 0..8");
@@ -421,8 +470,10 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = 
   int splits = d->split_k > 0 ? d->split_k : 1;
   if (bmn) splits = 1;  // split-K is built for the W[N,K] path
   if (bn == 0 || d->split_k == 0) {
-    plan_tiles(d->M, d->N, d->K, ez, swiglu, bmn, sms, bn, splits, d->split_k);
+    plan_tiles(batched ? d->M * bt->count : d->M, d->N, d->K, ez, swiglu, bmn, sms, bn, splits,
+               batched ? 1 : d->split_k);
   }
+  if (batched) splits = 1;
   if (bn != 64 && bn != 96 && bn != 128 && bn != 192 && bn != 256)
     return arg_fail("tile_n must be 64, 96, 128, 192 or 256");
   if (bmn && ez == 1 && bn < 128) return unsupported("tile_n 64 with int8 B[K,N]");
@@ -430,7 +481,7 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = 
   if ((bn == 96 || bn == 192) && bmn) return unsupported("tile_n 96 / 192 with B[K,N]");
   // Several 128-byte K blocks per TMA instruction when K is whole blocks:
   // the per-instruction cost of TMA, not bytes, limits small boxes.
-  const bool use3d = !bmn && (d->K * ez) % kKBytes == 0;
+  const bool use3d = !batched && !bmn && (d->K * ez) % kKBytes == 0;
   // CTA pairs (256 x 256 tiles, cta_group::2) for GEMMs with at least a wave
   // of pair tiles: each SM then ingests 1/3 fewer bytes per flop.
   bool pair = false;
@@ -462,7 +513,16 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = 
   const int out_w = swiglu ? bn / 2 : bn;
 
   CUtensorMap ta, tb;
-  if (use3d) {
+  if (batched) {
+    rc = make_tmap_batched(&ta, d->A, d->a_dtype, d->K, d->M, bt->count, d->lda * ez, bt->sa * ez, bk, kBM);
+    if (rc != HX_OK) return rc;
+    if (bmn)
+      rc = make_tmap_batched(&tb, d->B, d->b_dtype, d->N, d->K, bt->count, d->ldb * ez, bt->sb * ez,
+                             kKBytes / ez, bk);
+    else
+      rc = make_tmap_batched(&tb, d->B, d->b_dtype, d->K, d->N, bt->count, d->ldb * ez, bt->sb * ez, bk, bn);
+    if (rc != HX_OK) return rc;
+  } else if (use3d) {
     const uint64_t kblocks = static_cast<uint64_t>(d->K) / bk;
     rc = make_tmap3(&ta, d->A, d->a_dtype, bk, d->M, kblocks, d->lda, kBM, kbs);
     if (rc != HX_OK) return rc;
@@ -489,8 +549,12 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = 
   p.k_blocks = static_cast<int32_t>((d->K + bk - 1) / bk);
   p.n_half = static_cast<int32_t>(d->N);
   p.group_m = std::min<int32_t>(16, p.m_tiles);
-  const int64_t total = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
+  const int64_t item_tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
+  const int64_t total = item_tiles * (batched ? bt->count : 1);
   if (total > INT32_MAX) return unsupported("too many tiles");
+  p.batch = batched ? static_cast<int32_t>(bt->count) : 1;
+  p.batch_tiles = static_cast<int32_t>(item_tiles);
+  p.batch_rows = static_cast<int32_t>(d->M);
   p.total_tiles = static_cast<int32_t>(total);
   p.stages = stages;
   p.kbs = kbs;
@@ -500,6 +564,7 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = 
   p.timeout = d->timeout_cycles ? d->timeout_cycles : kDefaultTimeout;
   p.err_flag = d->error_flag;
   p.epi = make_epi(d);
+  if (batched) p.epi.M = static_cast<int32_t>(d->M * bt->count);  // flattened rows of C
   if (peers) {
     p.epi.n_peers = peers->n;
     for (int j = 0; j < peers->n; ++j) p.epi.peer_C[j] = peers->C[j];
@@ -1114,6 +1179,51 @@ const char *hx_last_error(void) { return hx::g_last_error.c_str(); }
 int hx_gemm(const hx_gemm_desc *d, void *stream) {
   hx::g_last_error.clear();
   return hx::gemm_impl(d, static_cast<cudaStream_t>(stream));
+}
+
+int hx_gemm_batched(const hx_gemm_desc *d, int64_t batch, int64_t stride_a, int64_t stride_b,
+                    int64_t stride_c, int64_t stride_r, void *stream) {
+  hx::g_last_error.clear();
+  if (!d || batch < 0 || stride_a < 0 || stride_b < 0 || stride_c < 0 || stride_r < 0)
+    return HX_E_INVALID_ARG;
+  if (batch == 0) return HX_OK;
+  if (d->epilogue == HX_EPI_SWIGLU) {
+    hx::g_last_error = "batched GEMM takes no SWIGLU epilogue";
+    return HX_E_UNSUPPORTED;
+  }
+  if (stride_c > 0 && stride_c < d->M * d->ldc && batch > 1) {
+    hx::g_last_error = "batch items of C overlap (stride_c < M * ldc)";
+    return HX_E_INVALID_ARG;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = hx::kNeedsLoop;
+  if (stride_b == 0) {
+    // One shared B: with A, C and residual items back to back this is one
+    // GEMM over batch * M rows.
+    if (stride_a == d->M * d->lda && stride_c == d->M * d->ldc &&
+        (!d->residual || stride_r == d->M * d->ldr) && batch * d->M <= INT32_MAX) {
+      hx_gemm_desc dm = *d;
+      dm.M = batch * d->M;
+      return hx::gemm_impl(&dm, s);
+    }
+  } else {
+    const hx::BatchSpec bt{batch, stride_a, stride_b, stride_c, stride_r};
+    rc = hx::gemm_impl(d, s, nullptr, &bt);
+  }
+  if (rc != hx::kNeedsLoop) return rc;
+  // Item by item: items whose rows are not whole tiles, or whose C rows are
+  // not back to back, or operands TMA cannot address as one 3-D view.
+  const int ez = hx::esize(d->a_dtype), cz = hx::esize(d->c_dtype);
+  for (int64_t i = 0; i < batch; ++i) {
+    hx_gemm_desc di = *d;
+    di.A = static_cast<const uint8_t *>(d->A) + i * stride_a * ez;
+    di.B = static_cast<const uint8_t *>(d->B) + i * stride_b * ez;
+    di.C = static_cast<uint8_t *>(d->C) + i * stride_c * cz;
+    if (d->residual) di.residual = static_cast<const uint8_t *>(d->residual) + i * stride_r * cz;
+    rc = hx::gemm_impl(&di, s);
+    if (rc != HX_OK) return rc;
+  }
+  return HX_OK;
 }
 
 int hx_matmul_f16f16_f32(int64_t n_row, int64_t n_col, int64_t n_inner, float *out,

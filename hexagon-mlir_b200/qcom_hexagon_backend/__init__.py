@@ -9,6 +9,7 @@ lib/libhx_gemm.so instead of the MLIR -> Hexagon LLVM -> DSP pipeline.
 
 from . import _lib
 from . import ops
-from .ops import W8A16Group, gemm, gemv_w8a16, linear, matmul, matmul_f16f16_f32, shards_to_rows
+from .ops import (W8A16Group, bmm, gemm, gemv_w8a16, linear, matmul, matmul_batched, matmul_f16f16_f32,
+                  shards_to_rows)
 
-__all__ = ["gemm", "gemv_w8a16", "linear", "matmul", "matmul_f16f16_f32", "shards_to_rows", "_lib"]
+__all__ = ["bmm", "matmul_batched", "gemm", "gemv_w8a16", "linear", "matmul", "matmul_f16f16_f32", "shards_to_rows", "_lib"]

@@ -110,6 +110,7 @@ class HxW8A16Proj(ctypes.Structure):
 _I64, _I32, _VP = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
 SIGNATURES = {
     "hx_gemm": (_I32, [ctypes.POINTER(HxGemmDesc), _VP]),
+    "hx_gemm_batched": (_I32, [ctypes.POINTER(HxGemmDesc), _I64, _I64, _I64, _I64, _I64, _VP]),
     "hx_sharded_gemm_gather_p2p": (_I32, [ctypes.POINTER(HxGemmDesc), _I32, _I32, _VP, _VP, _I32, _VP, _VP]),
     "hx_sharded_gemm_gather_ce": (_I32, [ctypes.POINTER(HxGemmDesc), _I32, _I32, _VP, _VP, _I32, _VP, _I32, _VP]),
     "hx_peer_handle_size": (_I32, []),

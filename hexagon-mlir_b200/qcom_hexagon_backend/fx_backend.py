@@ -29,6 +29,10 @@ inference-mode dropout, which it re-applies to the fused result:
   linear(x) + r   /   r + linear(x)  -> bias + residual epilogue
   silu(linear_g(x)) * linear_u(x)    -> SwiGLU epilogue over [W_g; W_u]
                                         (both without bias, same x)
+Batched products (torch.bmm / aten.bmm, and matmul with both operands of
+rank >= 3, e.g. attention's q @ k^T and p @ v) become one batched GEMM
+(hx_bmm), the batch_matmul / batch_matmul_transpose_b of
+ScheduleMatmulForHVXPass.cpp:105-167.
 Everything else in the graph runs unchanged (on the GPU, as torch ops).
 """
 
@@ -51,6 +55,7 @@ _LINEAR_FNS = (F.linear, torch._C._nn.linear, aten.linear.default)
 _ADDMM_FNS = (torch.addmm, aten.addmm.default)
 _MM_FNS = (torch.mm, aten.mm.default)
 _MATMUL_FNS = (torch.matmul, operator.matmul, aten.matmul.default)
+_BMM_FNS = (torch.bmm, aten.bmm.default)
 _GELU_FNS = (F.gelu, torch._C._nn.gelu, aten.gelu.default)
 _SILU_FNS = (F.silu, aten.silu.default)
 _ADD_FNS = (operator.add, torch.add, operator.iadd, aten.add.Tensor)
@@ -82,6 +87,14 @@ def hx_linear(x, weight, bias=None, residual=None, activation=None, weight_const
         residual = residual.reshape(*x.shape[:-1], n)
     return ops.linear(x, weight, bias, activation=activation, residual=residual, b_const=weight_const,
                       b_layout=b_layout)
+
+
+def hx_bmm(x, y):
+    """Batched product (torch.bmm / torch.matmul of rank >= 3 operands) on the
+    batched GEMM kernel: linalg.batch_matmul, or batch_matmul_transpose_b when
+    y is a transposed view."""
+    ops.chain_flush()
+    return ops.matmul_batched(x, y)
 
 
 def hx_swiglu(x, weight_gate_up):
@@ -403,9 +416,32 @@ def rewrite(gm: fx.GraphModule) -> fx.GraphModule:
         for dead in reversed(chain):
             graph.erase_node(dead)
         graph.erase_node(n)
+    _rewrite_batched(gm)
     graph.lint()
     gm.recompile()
     return gm
+
+
+def _rewrite_batched(gm: fx.GraphModule) -> None:
+    """bmm / matmul nodes whose operands are both batched (rank >= 3 known
+    from export metadata, or bmm itself) -> hx_bmm."""
+    graph = gm.graph
+    for n in list(graph.nodes):
+        if n.op != "call_function" or len(n.args) != 2 or n.kwargs:
+            continue
+        x, y = n.args
+        if n.target in _BMM_FNS:
+            pass
+        elif n.target in _MATMUL_FNS:
+            rx, ry = _rank(gm, x), _rank(gm, y)
+            if rx is None or ry is None or rx < 3 or ry < 3:
+                continue
+        else:
+            continue
+        with graph.inserting_before(n):
+            new = graph.call_function(hx_bmm, (x, y))
+        n.replace_all_uses_with(new)
+        graph.erase_node(n)
 
 
 def insert_chain_flushes(gm: fx.GraphModule) -> fx.GraphModule:
@@ -416,7 +452,7 @@ def insert_chain_flushes(gm: fx.GraphModule) -> fx.GraphModule:
     for n in list(graph.nodes):
         if n.op in ("placeholder", "get_attr"):
             continue
-        if n.op == "call_function" and (n.target in (hx_linear, hx_swiglu, ops.chain_flush)
+        if n.op == "call_function" and (n.target in (hx_linear, hx_swiglu, hx_bmm, ops.chain_flush)
                                         or n.target is operator.getitem):
             continue
         with graph.inserting_before(n):
@@ -427,7 +463,8 @@ def insert_chain_flushes(gm: fx.GraphModule) -> fx.GraphModule:
 
 
 def count_hx_calls(gm: fx.GraphModule) -> int:
-    return sum(1 for n in gm.graph.nodes if n.op == "call_function" and n.target in (hx_linear, hx_swiglu))
+    return sum(1 for n in gm.graph.nodes
+               if n.op == "call_function" and n.target in (hx_linear, hx_swiglu, hx_bmm))
 
 
 def capture(module: nn.Module, example_inputs=None, mode: str = "auto") -> fx.GraphModule:

@@ -346,6 +346,81 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, out: Optional[torch.Tensor] = No
     return gemm(a, b, b_layout="kn", out=out, out_dtype=out_dtype, **kw)
 
 
+def bmm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    *,
+    b_layout: str = "kn",
+    out: Optional[torch.Tensor] = None,
+    out_dtype: Optional[torch.dtype] = None,
+    epilogue: str = "none",
+    bias: Optional[torch.Tensor] = None,
+    residual: Optional[torch.Tensor] = None,
+    **kw,
+) -> torch.Tensor:
+    """Batched product out[i] = epilogue(a[i] @ B[i]) (hx_gemm_batched).
+
+    a: [batch, M, K] with unit stride along K (any row and item strides).
+    b: [batch, K, N] ("kn", linalg.batch_matmul) or [batch, N, K] ("nk",
+    batch_matmul_transpose_b), unit stride along the last dimension; a 2-D b
+    is shared by every item.  residual: [batch, M, N]; bias: [N], shared.
+    """
+    _check_cuda(a, "a")
+    if a.dim() != 3:
+        raise ValueError(f"a must be 3-D [batch, M, K], got {tuple(a.shape)}")
+    nb = a.shape[0]
+    shared = b.dim() == 2
+    if not shared and (b.dim() != 3 or b.shape[0] != nb):
+        raise ValueError(f"b must be [batch, ...] with batch {nb}, or 2-D, got {tuple(b.shape)}")
+    b0 = b if shared else b[0] if nb > 0 else b.new_empty(b.shape[1:])
+    M = a.shape[1]
+    N = (b0.shape[1] if b_layout == "kn" else b0.shape[0])
+    if out is None:
+        if out_dtype is None:
+            out_dtype = torch.int32 if (a.dtype == torch.int8 and epilogue == "none") else (
+                torch.float16 if a.dtype == torch.int8 else a.dtype)
+        out = torch.empty((nb, M, N), dtype=out_dtype, device=a.device)
+    elif tuple(out.shape) != (nb, M, N):
+        raise ValueError(f"out has shape {tuple(out.shape)}, expected {(nb, M, N)}")
+    if nb == 0:
+        return out
+    if residual is not None and tuple(residual.shape) != (nb, M, N):
+        raise ValueError("residual must be [batch, M, N]")
+    d, _, dev = make_desc(a[0], b0, b_layout=b_layout, out=out[0], epilogue=epilogue, bias=bias,
+                          residual=residual[0] if residual is not None else None, **kw)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.hx_gemm_batched(ctypes.byref(d), nb, a.stride(0), 0 if shared else b.stride(0),
+                                 out.stride(0), residual.stride(0) if residual is not None else 0,
+                                 ctypes.c_void_p(_stream_ptr(dev)))
+    _lib.check(rc, "hx_gemm_batched")
+    return out
+
+
+def matmul_batched(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    """torch.matmul for x [..., M, K] and y [..., K, N] with broadcast batch
+    dimensions.  A y whose K dimension has unit stride (a transposed view,
+    as in q @ k.transpose(-1, -2)) is read as W[N, K] items without a copy."""
+    if x.dim() < 2 or y.dim() < 2:
+        raise ValueError("matmul_batched needs operands of rank >= 2")
+    batch = torch.broadcast_shapes(x.shape[:-2], y.shape[:-2])
+    M, K = x.shape[-2], x.shape[-1]
+    N = y.shape[-1]
+    x3 = x.expand(*batch, M, K).reshape(-1, M, K)
+    if x3.stride(-1) != 1:
+        x3 = x3.contiguous()
+    if y.stride(-2) == 1 and y.stride(-1) != 1:  # [.., K, N] view of [.., N, K] memory
+        y3 = y.transpose(-1, -2).expand(*batch, N, K).reshape(-1, N, K)
+        layout = "nk"
+    else:
+        y3 = y.expand(*batch, K, N).reshape(-1, K, N)
+        layout = "kn"
+    if y3.stride(-1) != 1:
+        y3 = y3.contiguous()
+    out = bmm(x3, y3, b_layout=layout)
+    return out.reshape(*batch, M, N)
+
+
 def matmul_f16f16_f32(act: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """HexKL drop-in (hexkl_matmul_f16f16_f32, bin/runtime/src/HexKLAPI.cpp:15):
     out[f32, n_row x n_col] = act[f16, n_row x n_inner] @ W[f16, n_inner x n_col]."""

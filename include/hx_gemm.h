@@ -255,6 +255,19 @@ int hx_sharded_gemm_gather_p2p(const hx_gemm_desc *d, int rank, int world, void 
                                int32_t *const *flags, int32_t epoch, int32_t *error_flag,
                                void *stream);
 
+/* Batched GEMM: `batch` independent products with the descriptor's sizes,
+   dtypes, layout and epilogue; item i reads A + i*stride_a, B + i*stride_b
+   (and residual + i*stride_r) and writes C + i*stride_c, strides in
+   elements.  stride_b = 0 shares one B across the items (bias is always
+   shared).  This is linalg.batch_matmul (B[K,N] items, HX_B_KN) and
+   batch_matmul_transpose_b (B[N,K] items, HX_B_NK), the two forms
+   ScheduleMatmulForHVXPass.cpp:105-167 produces for batched contractions.
+   Items whose M is a multiple of 128, with C (and the residual) items back to
+   back (stride_c == M*ldc), run as one persistent launch over every item's
+   tiles; other shapes run item by item.  SWIGLU is not accepted. */
+int hx_gemm_batched(const hx_gemm_desc *d, int64_t batch, int64_t stride_a, int64_t stride_b,
+                    int64_t stride_c, int64_t stride_r, void *stream);
+
 /* The same result as hx_sharded_gemm_gather_p2p, with the transfer on the
    copy engines instead of the GEMM's epilogue: the GEMM runs in `chunks` row
    chunks (0 = automatic: min(6, M/2048); at most 16) on `stream` with every SM, and as each

@@ -123,3 +123,16 @@ def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
     u = np.asarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
     rounding = ((u >> 16) & 1) + 0x7FFF
     return ((u + rounding) >> 16).astype(np.uint16)
+
+
+def batch_matmul_f32(a, b, b_layout: str = "kn") -> np.ndarray:
+    """fp32 batched product of upcast operands: a [B,M,K]; b [B,K,N] ("kn",
+    linalg.batch_matmul) or [B,N,K] ("nk", batch_matmul_transpose_b, the
+    transpose fold of ScheduleMatmulForHVXPass.cpp:105-167); a 2-D b is
+    shared by every item.  Same arithmetic as matmul_f32, per item."""
+    A = as_f32(a)
+    B = as_f32(b)
+    if B.ndim == 2:
+        B = np.broadcast_to(B, (A.shape[0],) + B.shape)
+    Bk = np.swapaxes(B, -1, -2) if b_layout == "nk" else B
+    return np.matmul(A, Bk).astype(np.float32)

@@ -214,7 +214,8 @@ def test_batched_matmul_is_not_a_linear():
 
     q = torch.randn(2, 3, 5, 4)
     gm = FX.rewrite(FX.capture(B(), [q, q], "export"))
-    assert FX.count_hx_calls(gm) == 0
+    assert not any(n.target is FX.hx_linear for n in gm.graph.nodes)
+    assert sum(1 for n in gm.graph.nodes if n.target is FX.hx_bmm) == 1
 
 
 def test_training_dropout_blocks_fusion():
@@ -247,3 +248,43 @@ def test_hf_gpt2_lmhead_routes_every_linear():
     assert sum(n.kwargs.get("activation") == "gelu_tanh" for n in calls) == 12
     assert sum(n.kwargs.get("residual") is not None for n in calls) == 24
     assert not any("addmm" in str(n.target) for n in gm.graph.nodes)
+
+
+class _Attn(nn.Module):
+    def __init__(self, d=32, h=4):
+        super().__init__()
+        self.d, self.h = d, h
+        self.qkv = nn.Linear(d, 3 * d)
+        self.o = nn.Linear(d, d)
+
+    def forward(self, x):
+        B, S, _ = x.shape
+        q, k, v = self.qkv(x).split(self.d, dim=-1)
+        q = q.view(B, S, self.h, -1).transpose(1, 2)
+        k = k.view(B, S, self.h, -1).transpose(1, 2)
+        v = v.view(B, S, self.h, -1).transpose(1, 2)
+        p = torch.softmax(torch.matmul(q, k.transpose(-1, -2)), dim=-1)
+        return self.o(torch.matmul(p, v).transpose(1, 2).reshape(B, S, self.d))
+
+
+def test_rewrite_batched_matmuls_export():
+    """Attention's q @ k^T and p @ v (rank-4 operands) become hx_bmm calls; the
+    rewritten graph, with torch stand-ins for the kernels, computes the same."""
+    m = _Attn().eval()
+    x = torch.randn(2, 8, 32)
+    gm = FX.rewrite(FX.capture(m, [x], "export"))
+    assert sum(1 for n in gm.graph.nodes if n.op == "call_function" and n.target is FX.hx_bmm) == 2
+    assert FX.count_hx_calls(gm) == 4
+    for n in gm.graph.nodes:
+        if n.op == "call_function" and n.target is FX.hx_bmm:
+            n.target = torch.matmul
+    torch.testing.assert_close(_run_with_ref(gm, x), m(x), rtol=1e-5, atol=1e-5)
+
+
+def test_rewrite_torch_bmm_trace():
+    class M(nn.Module):
+        def forward(self, a, b):
+            return torch.bmm(a, b)
+
+    gm = FX.rewrite(fx.symbolic_trace(M()))
+    assert FX.count_hx_calls(gm) == 1
