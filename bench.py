@@ -413,7 +413,8 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
     odt = torch.int32 if int8 else torch.bfloat16
     esz = 4 if int8 else 2
     out = torch.empty(M, ns, dtype=odt, device=dev)
-    p2p = world > 1 and args.gather in ("p2p", "ce")
+    post_softmax = args.lm_post == "softmax"
+    p2p = world > 1 and args.gather in ("p2p", "ce") and not post_softmax
     transfer = "copy_engine" if args.gather == "ce" else "epilogue"
     main = torch.cuda.current_stream(dev)
 
@@ -429,13 +430,19 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
             if rank == 0:
                 print(f"{ex}; using NCCL", file=sys.stderr)
             p2p = False
-    chunks = 4 if (world > 1 and not p2p and M % 4 == 0) else 1
+    chunks = 4 if (world > 1 and not p2p and not post_softmax and M % 4 == 0) else 1
     mc = M // chunks
-    gathered = torch.empty(chunks, world * mc, ns, dtype=odt, device=dev) if (world > 1 and not p2p) else None
-    side = torch.cuda.Stream(dev) if (world > 1 and not p2p) else None
+    nccl_gather = world > 1 and not p2p and not post_softmax
+    gathered = torch.empty(chunks, world * mc, ns, dtype=odt, device=dev) if nccl_gather else None
+    side = torch.cuda.Stream(dev) if nccl_gather else None
     evs_c = [torch.cuda.Event() for _ in range(chunks)]
 
     def step():
+        if post_softmax:  # vocab-parallel softmax of the shards, in place: no logit gather
+            from qcom_hexagon_backend.sharding import vocab_parallel_softmax
+            gemm_only()
+            vocab_parallel_softmax(out, n1 - n0, out=out)
+            return
         if world == 1:
             return gemm_only()
         if p2p:  # one fused launch: the GEMM's epilogue writes every rank's buffer over NVLink
@@ -516,8 +523,9 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
     traffic = read_traffic("gemm_lmhead_int8.txt" if int8 else "gemm_lmhead.txt")
     if traffic is not None and args.lm_rows:
         traffic = None  # the recorded capture is of the full 16384-row launch
-    if world == 1:
-        # one GEMM launch per step: its average duration is the timed region's step time
+    if world == 1 or post_softmax:
+        # one GEMM launch per step (plus the softmax kernels with --lm-post
+        # softmax): the kernel's average duration is the timed step time
         per_launch = local_ms / args.steps
         achieved = my_flops / (per_launch / 1e3) / 1e12
         roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": unit,
@@ -549,6 +557,8 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) random-init weights)",
             "config": {"workload": f"LM head {M}x2048x50304 {dtname}, column-sharded (BASELINE config 5)",
                        "M": M, "K": K, "N": N, "shard_cols": ns,
+                       "post": ("vocab-parallel softmax of each rank's logit shard in place (stats all-gathered, "
+                                "[M, 2] floats per rank); no logit gather") if post_softmax else "logit gather",
                        "parallelism": f"tp{world} (N-sharded"
                        + ((", logits all-gathered into [world, M, N/world] by the GEMM's own epilogue "
                            "stores over NVLink (fused, hx_sharded_gemm_gather_p2p))" if p2p and transfer == "epilogue" else
@@ -564,10 +574,11 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                     "api": (f"sharding.P2PGather(transfer={transfer!r}).run" if p2p else "ops.gemm" + (" + NCCL all-gather" if world > 1 else ""))
                     + " with A copied from pinned host memory and this rank's logits shard copied back"},
-            "gpu_launches": args.steps * ((3 if transfer == "epilogue" else 2 + pg.last_chunks) if p2p else chunks),
+            "gpu_launches": args.steps * ((3 if transfer == "epilogue" else 2 + pg.last_chunks) if p2p else
+                                          (4 if post_softmax else chunks)),
             "roofline": roof,
             "clocks": clocks}
-    if world > 1:
+    if world > 1 and not post_softmax:
         recv = (world - 1) * M * ns * esz
         line["gather"] = {"bytes_received_per_rank": recv,
                           "nvlink_gbs_per_rank": round(recv / (ms / 1e3) / 1e9, 1),
@@ -626,6 +637,9 @@ def main(argv=None):
                     help="LM head at N>1: all-gather by the GEMM's epilogue stores over NVLink (p2p), "
                          "by copy-engine DMA of finished row chunks (ce), or by NCCL")
     ap.add_argument("--ce-chunks", type=int, default=0, help="row chunks of --gather ce (0 = automatic)")
+    ap.add_argument("--lm-post", choices=["gather", "softmax"], default="gather",
+                    help="LM head step: all-gather the logits (the config's definition) or a vocab-parallel "
+                         "softmax of each rank's shard (no gather)")
     ap.add_argument("--lm-dtype", choices=["bf16", "int8"], default="bf16",
                     help="LM head: bf16, or the int8 W8A8 variant (int32 accumulate)")
     ap.add_argument("--lm-rows", type=int, default=0,

@@ -40,6 +40,13 @@ struct EpiArgs {
   int32_t pre16;       // every operand the epilogue reads (scale, bias,
                        // residual) is 16-bit and 16-byte aligned: full
                        // 32-column chunks may be prefetched raw (Pre16)
+  // A normalisation of the rows of A folded into this GEMM (0 = none,
+  // 1 + HX_NORM_LAYER / HX_NORM_RMS): before the rest of the epilogue,
+  // acc = acc * rstd[m] - rstd[m] * mean[m] * col_sum[n] (the second term for
+  // LayerNorm only; SWIGLU: col_sum[N + n] for the up half).
+  int32_t norm;
+  const float *row_stats;  // [M][2]: mean, rstd
+  const float *col_sum;    // [N] (SWIGLU: [2N]) row sums of the folded weight
 };
 
 __device__ __forceinline__ float ld_as_float(const void *p, int dtype, int64_t i) {
@@ -309,8 +316,33 @@ __device__ __forceinline__ void epi_apply_t(const EpiArgs &e, float (&v)[32], co
 //   up[j]  : "up" accumulator for SWIGLU (ignored otherwise)
 // Every switch below is on a value uniform across the CTA; the per-element
 // loops inside each case are straight-line code.
+// The folded row normalisation of one 32-column chunk (e.norm != 0).
+__device__ __forceinline__ void epi_norm32(const EpiArgs &e, float (&v)[32], float (&up)[32], int m, int n0) {
+  if (m >= e.M) return;
+  const float2 st = reinterpret_cast<const float2 *>(e.row_stats)[m];
+  const float rstd = st.y;
+  if (e.norm == 1 + HX_NORM_RMS) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      v[j] *= rstd;
+      up[j] *= rstd;
+    }
+    return;
+  }
+  const float shift = rstd * st.x;
+  const bool sw = e.epi == HX_EPI_SWIGLU;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int n = n0 + j;
+    const float cs = n < e.N ? e.col_sum[n] : 0.f;
+    v[j] = v[j] * rstd - shift * cs;
+    if (sw) up[j] = up[j] * rstd - shift * (n < e.N ? e.col_sum[e.N + n] : 0.f);
+  }
+}
+
 __device__ __forceinline__ void epi_transform32(const EpiArgs &e, float (&v)[32],
-                                                const float (&up)[32], int m, int n0) {
+                                                float (&up)[32], int m, int n0) {
+  if (e.norm) epi_norm32(e, v, up, m, n0);
   const int epi = e.epi;
   if (epi == HX_EPI_NONE) return;
   if (epi == HX_EPI_SWIGLU) {
@@ -404,6 +436,15 @@ __device__ __forceinline__ void epi_store32(const EpiArgs &e, const float (&v)[3
 // Scalar form used by the CUDA-core fallback kernel.
 __device__ __forceinline__ float epi_scalar(const EpiArgs &e, float acc, float up, int m, int n) {
   const int epi = e.epi;
+  if (e.norm && m < e.M) {
+    const float2 st = reinterpret_cast<const float2 *>(e.row_stats)[m];
+    acc *= st.y;
+    up *= st.y;
+    if (e.norm == 1 + HX_NORM_LAYER) {
+      acc -= st.y * st.x * e.col_sum[n];
+      if (epi == HX_EPI_SWIGLU) up -= st.y * st.x * e.col_sum[e.N + n];
+    }
+  }
   if (epi == HX_EPI_SWIGLU) return silu(acc) * up;
   float v = acc;
   if (epi == HX_EPI_DEQUANT_SCALE) v *= ld_as_float(e.scale, e.scale_dtype, n);

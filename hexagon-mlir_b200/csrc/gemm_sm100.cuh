@@ -267,8 +267,9 @@ template <int BN, int BN_OUT, int KIND, bool SWIGLU>
 __device__ __forceinline__ void epi_row(const EpiArgs &e, uint32_t t_row, int m, int n_base, int c0,
                                         Pre16 &pf, uint8_t *stg) {
   // rows whose chunks also go to peers (fused all-gather) take the generic
-  // loop, which stores to every target; the specialised loop stores C only
-  if (!(e.pre16 && e.c_vec_ok && n_base + BN_OUT <= e.N) || e.n_peers > 0) {
+  // loop, which stores to every target; the specialised loop stores C only.
+  // So do GEMMs with a folded row normalisation.
+  if (!(e.pre16 && e.c_vec_ok && n_base + BN_OUT <= e.N) || e.n_peers > 0 || e.norm) {
     epi_row_generic<BN, BN_OUT, KIND, SWIGLU>(e, t_row, m, n_base, c0, stg);
     return;
   }

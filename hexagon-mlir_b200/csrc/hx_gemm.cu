@@ -367,6 +367,9 @@ EpiArgs make_epi(const hx_gemm_desc *d) {
   EpiArgs e;
   e.n_peers = 0;
   for (int i = 0; i < 7; ++i) e.peer_C[i] = nullptr;
+  e.norm = 0;
+  e.row_stats = nullptr;
+  e.col_sum = nullptr;
   e.C = d->C;
   e.ldc = d->ldc;
   e.bias = d->bias;
@@ -395,7 +398,13 @@ EpiArgs make_epi(const hx_gemm_desc *d) {
   return e;
 }
 
-int run_simt(const hx_gemm_desc *d, cudaStream_t s) {
+// A row normalisation folded into the GEMM (hx_gemm_norm).
+struct NormSpec {
+  int kind;
+  const float *row_stats, *col_sum;
+};
+
+int run_simt(const hx_gemm_desc *d, cudaStream_t s, const NormSpec *ns = nullptr) {
   SimtParams p;
   p.M = static_cast<int32_t>(d->M);
   p.N = static_cast<int32_t>(d->N);
@@ -408,6 +417,11 @@ int run_simt(const hx_gemm_desc *d, cudaStream_t s) {
   p.b_kn = d->b_layout == HX_B_KN;
   p.n_half = static_cast<int32_t>(d->N);
   p.epi = make_epi(d);
+  if (ns) {
+    p.epi.norm = 1 + ns->kind;
+    p.epi.row_stats = ns->row_stats;
+    p.epi.col_sum = ns->col_sum;
+  }
   dim3 grid((p.N + kSimtTile - 1) / kSimtTile, (p.M + kSimtTile - 1) / kSimtTile);
   if (grid.y > 65535) return unsupported("M too large for the CUDA-core kernel");
   const bool sw = d->epilogue == HX_EPI_SWIGLU;
@@ -436,7 +450,7 @@ struct BatchSpec {
 constexpr int kNeedsLoop = 2;  // internal: the batch is not one launch; run item by item
 
 int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = nullptr,
-              const BatchSpec *bt = nullptr) {
+              const BatchSpec *bt = nullptr, const NormSpec *ns = nullptr) {
   int rc = validate(d);
   if (rc != HX_OK) return rc;
   if (d->M == 0 || d->N == 0) return HX_OK;
@@ -463,7 +477,7 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = 
                             bt->count * d->M <= INT32_MAX && bt->count <= 65535;
     if (!one_launch) return kNeedsLoop;
   }
-  if (!tma_ok) return run_simt(d, s);
+  if (!tma_ok) return run_simt(d, s, ns);
 
   if (d->split_k < 0 || d->split_k > 8) return arg_fail("split_k must be 0..8");
   int bn = d->tile_n;
@@ -565,6 +579,11 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = 
   p.err_flag = d->error_flag;
   p.epi = make_epi(d);
   if (batched) p.epi.M = static_cast<int32_t>(d->M * bt->count);  // flattened rows of C
+  if (ns) {
+    p.epi.norm = 1 + ns->kind;
+    p.epi.row_stats = ns->row_stats;
+    p.epi.col_sum = ns->col_sum;
+  }
   if (peers) {
     p.epi.n_peers = peers->n;
     for (int j = 0; j < peers->n; ++j) p.epi.peer_C[j] = peers->C[j];
@@ -1224,6 +1243,21 @@ int hx_gemm_batched(const hx_gemm_desc *d, int64_t batch, int64_t stride_a, int6
     if (rc != HX_OK) return rc;
   }
   return HX_OK;
+}
+
+int hx_gemm_norm(const hx_gemm_desc *d, int kind, const float *row_stats, const float *col_sum,
+                 void *stream) {
+  hx::g_last_error.clear();
+  if (!d) return HX_E_INVALID_ARG;
+  if (kind != HX_NORM_LAYER && kind != HX_NORM_RMS) return HX_E_INVALID_ARG;
+  if (d->M > 0 && d->N > 0 && (!row_stats || (kind == HX_NORM_LAYER && !col_sum))) return HX_E_INVALID_ARG;
+  if (d->a_dtype != HX_F16 && d->a_dtype != HX_BF16) {
+    hx::g_last_error = "a folded normalisation needs f16 / bf16 inputs";
+    return HX_E_UNSUPPORTED;
+  }
+  if (d->epilogue == HX_EPI_DEQUANT_SCALE) return HX_E_UNSUPPORTED;
+  const hx::NormSpec ns{kind, row_stats, col_sum};
+  return hx::gemm_impl(d, static_cast<cudaStream_t>(stream), nullptr, nullptr, &ns);
 }
 
 int hx_matmul_f16f16_f32(int64_t n_row, int64_t n_col, int64_t n_inner, float *out,

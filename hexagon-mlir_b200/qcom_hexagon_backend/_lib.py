@@ -37,6 +37,8 @@ HX_GEMM_B_CONST = 1
 HX_GEMV_WEIGHTS_CONST = 1
 HX_GEMV_FORCE_CUDA_CORE = 2
 # epilogues
+HX_NORM_LAYER = 0
+HX_NORM_RMS = 1
 HX_EPI_NONE = 0
 HX_EPI_BIAS = 1
 HX_EPI_BIAS_GELU_TANH = 2
@@ -111,6 +113,12 @@ _I64, _I32, _VP = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
 SIGNATURES = {
     "hx_gemm": (_I32, [ctypes.POINTER(HxGemmDesc), _VP]),
     "hx_gemm_batched": (_I32, [ctypes.POINTER(HxGemmDesc), _I64, _I64, _I64, _I64, _I64, _VP]),
+    "hx_gemm_norm": (_I32, [ctypes.POINTER(HxGemmDesc), _I32, _VP, _VP, _VP]),
+    "hx_softmax": (_I32, [_VP, _I32, _I64, _I64, _I64, _VP, _I32, _I64, _I32, _VP]),
+    "hx_softmax_stats": (_I32, [_VP, _I32, _I64, _I64, _I64, _VP, _VP]),
+    "hx_softmax_combine": (_I32, [_VP, _I32, _I64, _VP, _VP]),
+    "hx_softmax_apply": (_I32, [_VP, _I32, _I64, _I64, _I64, _VP, _VP, _I32, _I64, _I32, _VP]),
+    "hx_row_norm_stats": (_I32, [_VP, _I32, _I64, _I64, _I64, _I32, ctypes.c_float, _VP, _VP]),
     "hx_sharded_gemm_gather_p2p": (_I32, [ctypes.POINTER(HxGemmDesc), _I32, _I32, _VP, _VP, _I32, _VP, _VP]),
     "hx_sharded_gemm_gather_ce": (_I32, [ctypes.POINTER(HxGemmDesc), _I32, _I32, _VP, _VP, _I32, _VP, _I32, _VP]),
     "hx_peer_handle_size": (_I32, []),

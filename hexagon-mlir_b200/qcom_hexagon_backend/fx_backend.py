@@ -68,13 +68,25 @@ _VIEW_METHODS = ("view", "reshape")
 _DROPOUT_FNS = (F.dropout, aten.dropout.default)
 
 
-def hx_linear(x, weight, bias=None, residual=None, activation=None, weight_const=False, b_layout="nk"):
+def hx_norm_stats(x, kind, eps):
+    """Row statistics of a LayerNorm / RMSNorm folded into the linears after it."""
+    ops.chain_flush()
+    return ops.row_norm_stats(x, kind, eps)
+
+
+def hx_linear(x, weight, bias=None, residual=None, activation=None, weight_const=False, b_layout="nk",
+              norm_kind=None, norm_stats=None, col_sum=None):
     """Fused linear used as the call_function target of rewritten nodes.
     weight: W[N,K] (b_layout "nk") or B[K,N] ("kn").  residual may have any
     shape whose last dimension is N and whose size is x's rows x N (the
     rewriter passes the consumer's operand, which can be the viewed shape).
     weight_const: the weight is a module parameter/buffer (constant while the
-    compiled forward runs), so the kernel may prefetch it early."""
+    compiled forward runs), so the kernel may prefetch it early.
+    norm_kind / norm_stats / col_sum: a LayerNorm / RMSNorm of x folded in
+    (weight and bias are then the folded ones, see ops.fold_norm_weight)."""
+    if norm_kind is not None:
+        return ops.linear(x, weight, bias, activation=activation, residual=residual, b_const=weight_const,
+                          b_layout=b_layout, norm=(norm_kind, norm_stats, col_sum))
     if residual is not None:
         n = weight.shape[0] if b_layout == "nk" else weight.shape[1]
         rows = x.numel() // x.shape[-1] if x.shape[-1] else 0
@@ -97,8 +109,11 @@ def hx_bmm(x, y):
     return ops.matmul_batched(x, y)
 
 
-def hx_swiglu(x, weight_gate_up):
+def hx_swiglu(x, weight_gate_up, norm_kind=None, norm_stats=None, col_sum=None):
     # the fused [gate; up] weight is a buffer the rewrite registered: constant
+    if norm_kind is not None:
+        return ops.linear(x, weight_gate_up, None, activation="swiglu", b_const=True,
+                          norm=(norm_kind, norm_stats, col_sum))
     return ops.linear(x, weight_gate_up, None, activation="swiglu", b_const=True)
 
 
@@ -417,9 +432,137 @@ def rewrite(gm: fx.GraphModule) -> fx.GraphModule:
             graph.erase_node(dead)
         graph.erase_node(n)
     _rewrite_batched(gm)
+    _fold_norms(gm)
     graph.lint()
     gm.recompile()
     return gm
+
+
+_LN_FNS = (F.layer_norm, aten.layer_norm.default)
+_RMS_FNS = (aten.rms_norm.default,) + ((F.rms_norm,) if hasattr(F, "rms_norm") else ())
+
+
+def _norm_site(gm, n: fx.Node):
+    """(kind, x, gamma, beta, eps) of a LayerNorm / RMSNorm over the last
+    dimension whose affine parameters are constants (get_attr names or None)."""
+    def attr_or_none(v):
+        if v is None:
+            return True, None
+        if isinstance(v, fx.Node) and v.op == "get_attr":
+            return True, v.target
+        return False, None
+
+    if n.op == "call_module":
+        mod = gm.get_submodule(n.target)
+        if isinstance(mod, nn.LayerNorm) and len(mod.normalized_shape) == 1 and len(n.args) == 1:
+            return ("layer", n.args[0], n.target + ".weight" if mod.weight is not None else None,
+                    n.target + ".bias" if mod.bias is not None else None, float(mod.eps))
+        if hasattr(nn, "RMSNorm") and isinstance(mod, nn.RMSNorm) and len(mod.normalized_shape) == 1 \
+                and mod.eps is not None and len(n.args) == 1:
+            return ("rms", n.args[0], n.target + ".weight" if mod.weight is not None else None, None, float(mod.eps))
+        return None
+    if n.op != "call_function":
+        return None
+    if n.target in _LN_FNS:
+        args = list(n.args) + [None] * (5 - len(n.args))
+        x, shape = args[0], n.kwargs.get("normalized_shape", args[1])
+        w, b = n.kwargs.get("weight", args[2]), n.kwargs.get("bias", args[3])
+        eps = n.kwargs.get("eps", args[4] if args[4] is not None else 1e-5)
+        kind = "layer"
+    elif n.target in _RMS_FNS:
+        args = list(n.args) + [None] * (4 - len(n.args))
+        x, shape = args[0], n.kwargs.get("normalized_shape", args[1])
+        w, b, eps = n.kwargs.get("weight", args[2]), None, n.kwargs.get("eps", args[3])
+        kind = "rms"
+        if eps is None:
+            return None  # dtype-dependent default: not known from the graph
+    else:
+        return None
+    if not isinstance(shape, (list, tuple)) or len(shape) != 1 or not isinstance(eps, (int, float)):
+        return None
+    ok_w, wname = attr_or_none(w)
+    ok_b, bname = attr_or_none(b)
+    if not (ok_w and ok_b):
+        return None
+    return kind, x, wname, bname, float(eps)
+
+
+def _fold_norms(gm: fx.GraphModule) -> None:
+    """norm(x) whose every use reaches (through reshapes) the activation input
+    of a fused linear with constant W[N,K] weights -> row statistics of x plus
+    linears over x with gamma / beta folded into their weights and bias; the
+    normalised activation is never materialised."""
+    graph = gm.graph
+    cache = {}
+    for n in list(graph.nodes):
+        site = _norm_site(gm, n)
+        if site is None:
+            continue
+        kind, x, gname, bname, eps = site
+        uses = []  # (chain of reshapes, consumer)
+        ok = True
+        for u in _users(n):
+            chain, cur = [], u
+            while _is_transparent(gm, cur) and len(_users(cur)) == 1 and cur.args and \
+                    (cur.args[0] is n or (chain and cur.args[0] is chain[-1])):
+                chain.append(cur)
+                cur = _users(cur)[0]
+            src = chain[-1] if chain else n
+            if src in cur.args[1:] or any(v is src for v in cur.kwargs.values()):
+                ok = False  # the normalised value is needed itself (e.g. as a residual)
+                break
+            if cur.op == "call_function" and cur.target is hx_linear and cur.args[0] is src and \
+                    cur.kwargs.get("b_layout", "nk") == "nk" and cur.kwargs.get("norm_kind") is None and \
+                    isinstance(cur.args[1], fx.Node) and cur.args[1].op == "get_attr" and \
+                    (cur.args[2] is None or (isinstance(cur.args[2], fx.Node) and cur.args[2].op == "get_attr")):
+                uses.append((chain, cur))
+            elif cur.op == "call_function" and cur.target is hx_swiglu and cur.args[0] is src and \
+                    len(cur.args) == 2 and isinstance(cur.args[1], fx.Node) and cur.args[1].op == "get_attr":
+                uses.append((chain, cur))
+            else:
+                ok = False
+                break
+        if not ok or not uses:
+            continue
+        gamma = _get_attr(gm, gname).detach() if gname else None
+        beta = _get_attr(gm, bname).detach() if bname else None
+        with graph.inserting_before(n):
+            stats = graph.call_function(hx_norm_stats, (x, kind, eps))
+        for chain, lin in uses:
+            wname = lin.args[1].target
+            bias_node = lin.args[2] if lin.target is hx_linear else None
+            key = (wname, bias_node.target if bias_node is not None else None, gname, bname, kind)
+            if key not in cache:
+                w = _get_attr(gm, wname).detach()
+                b = _get_attr(gm, bias_node.target).detach() if bias_node is not None else None
+                wf, cs, bf = ops.fold_norm_weight(w, b, gamma, beta, kind)
+                i = len(cache)
+                gm.register_buffer(f"_hx_nw{i}", wf)
+                if cs is not None:
+                    gm.register_buffer(f"_hx_ncs{i}", cs)
+                if bf is not None:
+                    gm.register_buffer(f"_hx_nb{i}", bf)
+                cache[key] = (f"_hx_nw{i}", f"_hx_ncs{i}" if cs is not None else None,
+                              f"_hx_nb{i}" if bf is not None else None)
+            wn, csn, bn = cache[key]
+            with graph.inserting_before(lin):
+                mapping, last = {n: x}, x
+                for cn in chain:
+                    last = graph.node_copy(cn, lambda a: mapping.get(a, a))
+                    mapping[cn] = last
+                wnode = graph.get_attr(wn)
+                csnode = graph.get_attr(csn) if csn else None
+                bnode = graph.get_attr(bn) if bn else None
+            new_args = list(lin.args)
+            new_args[0] = last
+            new_args[1] = wnode
+            if lin.target is hx_linear:
+                new_args[2] = bnode
+            lin.args = tuple(new_args)
+            lin.kwargs = dict(lin.kwargs, norm_kind=kind, norm_stats=stats, col_sum=csnode)
+            for cn in reversed(chain):
+                graph.erase_node(cn)
+        graph.erase_node(n)
 
 
 def _rewrite_batched(gm: fx.GraphModule) -> None:
@@ -452,7 +595,7 @@ def insert_chain_flushes(gm: fx.GraphModule) -> fx.GraphModule:
     for n in list(graph.nodes):
         if n.op in ("placeholder", "get_attr"):
             continue
-        if n.op == "call_function" and (n.target in (hx_linear, hx_swiglu, hx_bmm, ops.chain_flush)
+        if n.op == "call_function" and (n.target in (hx_linear, hx_swiglu, hx_bmm, hx_norm_stats, ops.chain_flush)
                                         or n.target is operator.getitem):
             continue
         with graph.inserting_before(n):

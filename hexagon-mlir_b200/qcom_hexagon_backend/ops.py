@@ -79,9 +79,15 @@ def gemm(
     timeout_cycles: int = 0,
     split_k: int = 0,
     b_const: bool = False,
+    norm: Optional[tuple] = None,
 ) -> torch.Tensor:
     """out = epilogue(a @ B) with B = b.T (b_layout "nk", b is W[N,K]) or
     B = b (b_layout "kn", b is [K,N]).
+
+    norm: (kind, row_stats, col_sum) folds a LayerNorm / RMSNorm of a's rows
+    into the GEMM (hx_gemm_norm): b is then the folded weight W * gamma,
+    row_stats the [M, 2] float32 output of row_norm_stats(a) and col_sum the
+    float32 row sums of b (see fold_norm_weight).
 
     For epilogue "swiglu", b is the fused [gate; up] weight of 2N rows and
     out = silu(a @ gate.T) * (a @ up.T) has N columns.  b_const: b is a
@@ -92,6 +98,25 @@ def gemm(
                             bias=bias, residual=residual, scale=scale, tile_n=tile_n, stages=stages,
                             max_ctas=max_ctas, force_simt=force_simt, error_flag=error_flag,
                             timeout_cycles=timeout_cycles, split_k=split_k, b_const=b_const)
+    if norm is not None:
+        kind, stats, col_sum = norm
+        kind = _NORM_KINDS[kind] if isinstance(kind, str) else int(kind)
+        _check_cuda(stats, "row_stats", dev)
+        if stats.dtype != torch.float32 or tuple(stats.shape) != (a.shape[0], 2) or not stats.is_contiguous():
+            raise ValueError("row_stats must be a contiguous float32 [M, 2] tensor")
+        if kind == _lib.HX_NORM_LAYER:
+            want = 2 * d.N if epilogue == "swiglu" else d.N
+            _check_cuda(col_sum, "col_sum", dev)
+            if col_sum.dtype != torch.float32 or col_sum.numel() != want or not col_sum.is_contiguous():
+                raise ValueError(f"col_sum must be a contiguous float32 vector of {want}")
+        chain_flush()
+        lib = _lib.load()
+        with torch.cuda.device(dev):
+            rc = lib.hx_gemm_norm(ctypes.byref(d), kind, ctypes.c_void_p(stats.data_ptr()),
+                                  ctypes.c_void_p(col_sum.data_ptr() if col_sum is not None else 0),
+                                  ctypes.c_void_p(_stream_ptr(dev)))
+        _lib.check(rc, "hx_gemm_norm")
+        return out
     rec = _recorder
     if rec is not None and rec.device == dev:
         if rec.accepts(d, a, b, residual, b_layout, tile_n, stages, max_ctas, force_simt):
@@ -344,6 +369,122 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, out: Optional[torch.Tensor] = No
            out_dtype: Optional[torch.dtype] = None, **kw) -> torch.Tensor:
     """C = A @ B with B stored [K, N] (plain linalg.matmul / tl.dot)."""
     return gemm(a, b, b_layout="kn", out=out, out_dtype=out_dtype, **kw)
+
+
+_NORM_KINDS = {"layer": _lib.HX_NORM_LAYER, "rms": _lib.HX_NORM_RMS}
+
+
+def row_norm_stats(x: torch.Tensor, kind: str = "layer", eps: float = 1e-5) -> torch.Tensor:
+    """[M, 2] float32 per-row {mean, 1/sqrt(var + eps)} (kind "layer",
+    F.layer_norm's statistics) or {0, 1/sqrt(mean(x^2) + eps)} ("rms") of the
+    last dimension of x (hx_row_norm_stats)."""
+    _check_cuda(x, "x")
+    x2 = x.reshape(-1, x.shape[-1])
+    ld = _row_major_2d(x2, "x")
+    stats = torch.empty((x2.shape[0], 2), dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        rc = lib.hx_row_norm_stats(ctypes.c_void_p(x2.data_ptr()), _dtype_code(x2, "x"), x2.shape[0], x2.shape[1],
+                                   ld, _NORM_KINDS[kind], ctypes.c_float(eps), ctypes.c_void_p(stats.data_ptr()),
+                                   ctypes.c_void_p(_stream_ptr(x.device)))
+    _lib.check(rc, "hx_row_norm_stats")
+    return stats
+
+
+def fold_norm_weight(weight: torch.Tensor, bias: Optional[torch.Tensor], gamma: Optional[torch.Tensor],
+                     beta: Optional[torch.Tensor], kind: str = "layer"):
+    """Fold a norm's affine parameters into the linear layer after it (done
+    once, at compile time): returns (W' = W * gamma in W's dtype, col_sum =
+    float32 row sums of W' as stored, bias' = bias + W @ beta in float32, or
+    None).  With these, linear(norm(x)) = linear_norm(x, W', col_sum, bias')."""
+    w32 = weight.float()
+    if gamma is not None:
+        w32 = w32 * gamma.float()[None, :]
+    wf = w32.to(weight.dtype).contiguous()
+    col_sum = wf.float().sum(1).contiguous() if kind == "layer" else None
+    b = bias.float() if bias is not None else None
+    if beta is not None and kind == "layer":
+        wb = weight.float() @ beta.float()
+        b = wb if b is None else b + wb
+    return wf, col_sum, (b.contiguous() if b is not None else None)
+
+
+def linear_norm(x: torch.Tensor, weight: torch.Tensor, col_sum: Optional[torch.Tensor],
+                bias: Optional[torch.Tensor], stats: torch.Tensor, kind: str = "layer", *,
+                activation: Optional[str] = None, residual: Optional[torch.Tensor] = None,
+                **kw) -> torch.Tensor:
+    """linear(norm(x)) with the norm folded (weights from fold_norm_weight,
+    stats from row_norm_stats(x))."""
+    return linear(x, weight, bias, activation=activation, residual=residual, norm=(kind, stats, col_sum), **kw)
+
+
+def _softmax_dtypes(x, out, out_dtype):
+    if out is None:
+        out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    return out
+
+
+def softmax(x: torch.Tensor, *, log: bool = False, out: Optional[torch.Tensor] = None,
+            out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """Softmax (log-softmax with log=True) over the last dimension (hx_softmax)."""
+    _check_cuda(x, "x")
+    x2 = x.reshape(-1, x.shape[-1])
+    ldx = _row_major_2d(x2, "x")
+    out = _softmax_dtypes(x, out, out_dtype)
+    o2 = out.view(-1, out.shape[-1])
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        rc = lib.hx_softmax(ctypes.c_void_p(x2.data_ptr()), _dtype_code(x2, "x"), x2.shape[0], x2.shape[1], ldx,
+                            ctypes.c_void_p(o2.data_ptr()), _dtype_code(o2, "out"), _row_major_2d(o2, "out"),
+                            1 if log else 0, ctypes.c_void_p(_stream_ptr(x.device)))
+    _lib.check(rc, "hx_softmax")
+    return out
+
+
+def softmax_stats(x: torch.Tensor) -> torch.Tensor:
+    """[M, 2] float32 {row max, sum of exp(x - max)} of a 2-D x (hx_softmax_stats)."""
+    _check_cuda(x, "x")
+    ldx = _row_major_2d(x, "x")
+    st = torch.empty((x.shape[0], 2), dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        rc = lib.hx_softmax_stats(ctypes.c_void_p(x.data_ptr()), _dtype_code(x, "x"), x.shape[0], x.shape[1], ldx,
+                                  ctypes.c_void_p(st.data_ptr()), ctypes.c_void_p(_stream_ptr(x.device)))
+    _lib.check(rc, "hx_softmax_stats")
+    return st
+
+
+def softmax_combine(stats_all: torch.Tensor) -> torch.Tensor:
+    """[world, M, 2] per-rank pairs -> [M, 2] global {max, sum} (hx_softmax_combine)."""
+    _check_cuda(stats_all, "stats_all")
+    if stats_all.dtype != torch.float32 or stats_all.dim() != 3 or not stats_all.is_contiguous():
+        raise ValueError("stats_all must be a contiguous float32 [world, M, 2] tensor")
+    world, M, _ = stats_all.shape
+    st = torch.empty((M, 2), dtype=torch.float32, device=stats_all.device)
+    lib = _lib.load()
+    with torch.cuda.device(stats_all.device):
+        rc = lib.hx_softmax_combine(ctypes.c_void_p(stats_all.data_ptr()), world, M, ctypes.c_void_p(st.data_ptr()),
+                                    ctypes.c_void_p(_stream_ptr(stats_all.device)))
+    _lib.check(rc, "hx_softmax_combine")
+    return st
+
+
+def softmax_apply(x: torch.Tensor, stats: torch.Tensor, *, log: bool = False, out: Optional[torch.Tensor] = None,
+                  out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """Softmax of a 2-D x with given [M, 2] row {max, sum} (hx_softmax_apply)."""
+    _check_cuda(x, "x")
+    ldx = _row_major_2d(x, "x")
+    if stats.dtype != torch.float32 or tuple(stats.shape) != (x.shape[0], 2) or not stats.is_contiguous():
+        raise ValueError("stats must be a contiguous float32 [M, 2] tensor")
+    out = _softmax_dtypes(x, out, out_dtype)
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        rc = lib.hx_softmax_apply(ctypes.c_void_p(x.data_ptr()), _dtype_code(x, "x"), x.shape[0], x.shape[1], ldx,
+                                  ctypes.c_void_p(stats.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                                  _dtype_code(out, "out"), _row_major_2d(out, "out"), 1 if log else 0,
+                                  ctypes.c_void_p(_stream_ptr(x.device)))
+    _lib.check(rc, "hx_softmax_apply")
+    return out
 
 
 def bmm(

@@ -64,6 +64,30 @@ def gather_columns(local: torch.Tensor, N: int, group=None) -> torch.Tensor:
     return rows_from_shards(gathered, N)
 
 
+def vocab_parallel_softmax(local: torch.Tensor, n_valid: Optional[int] = None, group=None, *,
+                           log: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Softmax over the full vocabulary of column-sharded logits, without
+    gathering them: local is this rank's [M, Ns] shard (its first n_valid
+    columns are real; the padding of a short last shard is left out).  Each
+    rank reduces its rows to {max, sum exp}, the ranks all-gather those
+    [M, 2] floats (8 bytes a row), every rank combines them into the global
+    pair and normalises its own columns.  Returns this rank's [M, n_valid]
+    probabilities (log-probabilities with log=True); out may be `local`
+    itself (in place)."""
+    x = local if n_valid is None or n_valid == local.shape[1] else local[:, :n_valid]
+    st = ops.softmax_stats(x)
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if world > 1:
+        all_st = torch.empty((world,) + tuple(st.shape), dtype=st.dtype, device=st.device)
+        dist.all_gather_into_tensor(all_st, st, group=group)
+    else:
+        all_st = st.unsqueeze(0)
+    glob = ops.softmax_combine(all_st)
+    if out is not None and out.shape != x.shape:
+        out = out[:, : x.shape[1]]
+    return ops.softmax_apply(x, glob, log=log, out=out)
+
+
 class NcclComm:
     """An NCCL communicator owned by libhx_gemm (for hx_sharded_gemm_allgather).
     Rank 0 creates the unique id; torch.distributed broadcasts it."""

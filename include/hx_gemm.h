@@ -268,6 +268,56 @@ int hx_sharded_gemm_gather_p2p(const hx_gemm_desc *d, int rank, int world, void 
 int hx_gemm_batched(const hx_gemm_desc *d, int64_t batch, int64_t stride_a, int64_t stride_b,
                     int64_t stride_c, int64_t stride_r, void *stream);
 
+/* ---- row kernels either side of the linear layer ---------------------- */
+
+/* Softmax over rows of x[M, N] (dtype HX_F16 / HX_BF16 / HX_F32, row stride
+   ldx), written to y (y_dtype, row stride ldy): y = exp(x - max) / sum, or the
+   log-softmax x - max - log(sum) when log_softmax != 0.  One pass over x when
+   a row fits in shared memory (200 KB: N <= 102400 for 16-bit x), else two.  Reference: the row
+   softmax of test/python/triton/test_softmax.py and the online (running max,
+   rescaled sum) softmax of test/python/triton/test_online_softmax.py. */
+int hx_softmax(const void *x, int dtype, int64_t M, int64_t N, int64_t ldx, void *y, int y_dtype,
+               int64_t ldy, int log_softmax, void *stream);
+
+/* Vocab-parallel softmax, in three steps, for logits split by column across
+   ranks (each rank holds x[M, N_local]):
+     hx_softmax_stats    per row of the local shard: stats[m] = {max, sum of
+                         exp(x - max)} (float pairs, [M][2]);
+     (the caller exchanges the [M][2] stats of all ranks: [world][M][2])
+     hx_softmax_combine  the global {max, sum} per row from every rank's pair;
+     hx_softmax_apply    the local shard's softmax (or log-softmax) with the
+                         global pair.
+   The logits themselves never cross GPUs. */
+int hx_softmax_stats(const void *x, int dtype, int64_t M, int64_t N, int64_t ldx, float *stats,
+                     void *stream);
+int hx_softmax_combine(const float *stats_all, int world, int64_t M, float *stats, void *stream);
+int hx_softmax_apply(const void *x, int dtype, int64_t M, int64_t N, int64_t ldx, const float *stats,
+                     void *y, int y_dtype, int64_t ldy, int log_softmax, void *stream);
+
+/* Row statistics of a normalisation that the next GEMM folds in:
+   kind HX_NORM_LAYER: stats[m] = {mean, 1/sqrt(var + eps)} (biased variance,
+   F.layer_norm); HX_NORM_RMS: stats[m] = {0, 1/sqrt(mean(x^2) + eps)}
+   (F.rms_norm).  Reference: test/python/triton/test_layer_norm.py,
+   test_rms_norm.py. */
+#define HX_NORM_LAYER 0
+#define HX_NORM_RMS 1
+int hx_row_norm_stats(const void *x, int dtype, int64_t M, int64_t K, int64_t ldx, int kind, float eps,
+                      float *stats, void *stream);
+
+/* GEMM of the un-normalised rows of A with a LayerNorm / RMSNorm folded in:
+   with gamma and beta folded into the weight beforehand,
+     W'[n,k] = W[n,k] * gamma[k],   col_sum[n] = sum_k W'[n,k],
+     bias'[n] = bias[n] + sum_k W[n,k] * beta[k]   (LayerNorm),
+   the result equals  epilogue(norm(A) . W^T)  as
+     acc * rstd[m] - rstd[m] * mean[m] * col_sum[n]   (RMSNorm: acc * rstd[m])
+   followed by the descriptor's epilogue with bias'.  d->B is W'; row_stats
+   comes from hx_row_norm_stats on A.  SWIGLU: col_sum has 2N entries (gate,
+   then up).  The normalised activation is never written to memory.
+   Reference: the norm kernels of test/python/triton/test_layer_norm.py and
+   test_rms_norm.py, which run as a separate pass before the matmul. */
+int hx_gemm_norm(const hx_gemm_desc *d, int kind, const float *row_stats, const float *col_sum,
+                 void *stream);
+
 /* The same result as hx_sharded_gemm_gather_p2p, with the transfer on the
    copy engines instead of the GEMM's epilogue: the GEMM runs in `chunks` row
    chunks (0 = automatic: min(6, M/2048); at most 16) on `stream` with every SM, and as each

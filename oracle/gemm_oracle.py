@@ -136,3 +136,40 @@ def batch_matmul_f32(a, b, b_layout: str = "kn") -> np.ndarray:
         B = np.broadcast_to(B, (A.shape[0],) + B.shape)
     Bk = np.swapaxes(B, -1, -2) if b_layout == "nk" else B
     return np.matmul(A, Bk).astype(np.float32)
+
+
+def softmax_ref(x, log: bool = False) -> np.ndarray:
+    """Row softmax (or log-softmax) in fp64 of upcast x: the golden of
+    test/python/triton/test_softmax.py / test_online_softmax.py
+    (torch.nn.functional.softmax(x, dim=1))."""
+    X = np.asarray(x, dtype=np.float64)
+    mx = X.max(axis=-1, keepdims=True)
+    e = np.exp(X - mx)
+    s = e.sum(axis=-1, keepdims=True)
+    return (X - mx - np.log(s)) if log else e / s
+
+
+def norm_ref(x, kind: str = "layer", gamma=None, beta=None, eps: float = 1e-5) -> np.ndarray:
+    """F.layer_norm (biased variance) or F.rms_norm over the last dimension, in
+    fp64: the goldens of test/python/triton/test_layer_norm.py and
+    test_rms_norm.py."""
+    X = np.asarray(x, dtype=np.float64)
+    if kind == "layer":
+        mu = X.mean(-1, keepdims=True)
+        var = ((X - mu) ** 2).mean(-1, keepdims=True)
+        Y = (X - mu) / np.sqrt(var + eps)
+    else:
+        Y = X / np.sqrt((X * X).mean(-1, keepdims=True) + eps)
+    if gamma is not None:
+        Y = Y * np.asarray(gamma, np.float64)
+    if beta is not None:
+        Y = Y + np.asarray(beta, np.float64)
+    return Y
+
+
+def norm_linear_ref(x, w, *, kind="layer", gamma=None, beta=None, eps=1e-5, epilogue="none", bias=None,
+                    residual=None) -> np.ndarray:
+    """epilogue(norm(x) @ W^T): the norm in fp64, rounded to nothing, then the
+    fp32 linear oracle.  (Unfused reference order: norm pass, then matmul.)"""
+    y = norm_ref(x, kind, gamma, beta, eps).astype(np.float32)
+    return linear_ref(y, w, epilogue=epilogue, bias=bias, residual=residual)

@@ -288,3 +288,108 @@ def test_rewrite_torch_bmm_trace():
 
     gm = FX.rewrite(fx.symbolic_trace(M()))
     assert FX.count_hx_calls(gm) == 1
+
+
+def _ref_stats(x, kind, eps):
+    x2 = x.reshape(-1, x.shape[-1]).float()
+    mu = x2.mean(-1) if kind == "layer" else torch.zeros(x2.shape[0])
+    var = x2.var(-1, unbiased=False) if kind == "layer" else (x2 * x2).mean(-1)
+    return torch.stack([mu, torch.rsqrt(var + eps)], -1)
+
+
+def _ref_linear_norm(x, weight, bias=None, residual=None, activation=None, weight_const=False, b_layout="nk",
+                     norm_kind=None, norm_stats=None, col_sum=None):
+    x2 = x.reshape(-1, x.shape[-1]).float()
+    y = x2 @ (weight.float() if b_layout == "kn" else weight.float().t())
+    if norm_kind is not None:
+        y = y * norm_stats[:, 1:2]
+        if norm_kind == "layer":
+            y = y - (norm_stats[:, 1:2] * norm_stats[:, 0:1]) * col_sum[None, :]
+    if bias is not None:
+        y = y + bias.float()
+    if activation == "gelu_tanh":
+        y = F.gelu(y, approximate="tanh")
+    elif activation == "swiglu":
+        n = y.shape[-1] // 2
+        y = F.silu(y[:, :n]) * y[:, n:]
+    if residual is not None:
+        y = y + residual.reshape(y.shape).float()
+    return y.reshape(*x.shape[:-1], y.shape[-1])
+
+
+def _run_norm_ref(gm, *args):
+    for n in gm.graph.nodes:
+        if n.op == "call_function" and n.target is FX.hx_linear:
+            n.target = _ref_linear_norm
+        elif n.op == "call_function" and n.target is FX.hx_norm_stats:
+            n.target = _ref_stats
+        elif n.op == "call_function" and n.target is FX.hx_swiglu:
+            n.target = lambda x, w, norm_kind=None, norm_stats=None, col_sum=None: _ref_linear_norm(
+                x, w, activation="swiglu", norm_kind=norm_kind, norm_stats=norm_stats, col_sum=col_sum)
+    gm.recompile()
+    return gm(*args)
+
+
+class _LNBlock(nn.Module):
+    def __init__(self, d=32):
+        super().__init__()
+        self.ln = nn.LayerNorm(d)
+        self.up = nn.Linear(d, 64)
+        self.qkv = nn.Linear(d, 48)
+        with torch.no_grad():
+            self.ln.weight.uniform_(0.5, 1.5)
+            self.ln.bias.uniform_(-0.3, 0.3)
+
+    def forward(self, x):
+        h = self.ln(x)
+        return F.gelu(self.up(h), approximate="tanh").sum(-1) + self.qkv(h).sum(-1)
+
+
+@pytest.mark.parametrize("mode", ["trace", "export"])
+def test_fold_layernorm_into_linears(mode):
+    m = _LNBlock().eval()
+    x = torch.randn(3, 7, 32) * 2 + 1
+    gm = FX.rewrite(FX.capture(m, [x], mode))
+    assert sum(1 for n in gm.graph.nodes if n.target is FX.hx_norm_stats) == 1
+    assert not any("layer_norm" in str(n.target) or (n.op == "call_module" and "ln" in str(n.target))
+                   for n in gm.graph.nodes)
+    folded = [n for n in gm.graph.nodes if n.target is FX.hx_linear]
+    assert len(folded) == 2 and all(n.kwargs.get("norm_kind") == "layer" for n in folded)
+    torch.testing.assert_close(_run_norm_ref(gm, x), m(x), rtol=1e-4, atol=1e-4)
+
+
+def test_fold_rmsnorm_into_swiglu():
+    class Qwenish(nn.Module):
+        def __init__(self, d=32, f=40):
+            super().__init__()
+            self.norm = nn.RMSNorm(d, eps=1e-6)
+            self.gate = nn.Linear(d, f, bias=False)
+            self.up = nn.Linear(d, f, bias=False)
+            with torch.no_grad():
+                self.norm.weight.uniform_(0.5, 1.5)
+
+        def forward(self, x):
+            h = self.norm(x)
+            return F.silu(self.gate(h)) * self.up(h)
+
+    m = Qwenish().eval()
+    x = torch.randn(5, 32)
+    gm = FX.rewrite(fx.symbolic_trace(m))
+    sw = [n for n in gm.graph.nodes if n.target is FX.hx_swiglu]
+    assert len(sw) == 1 and sw[0].kwargs.get("norm_kind") == "rms"
+    torch.testing.assert_close(_run_norm_ref(gm, x), m(x), rtol=1e-4, atol=1e-4)
+
+
+def test_norm_with_other_user_not_folded():
+    class M(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.ln = nn.LayerNorm(16)
+            self.l = nn.Linear(16, 16)
+
+        def forward(self, x):
+            h = self.ln(x)
+            return self.l(h) + h  # h itself is needed: the norm stays
+
+    gm = FX.rewrite(fx.symbolic_trace(M()))
+    assert not any(n.target is FX.hx_norm_stats for n in gm.graph.nodes)

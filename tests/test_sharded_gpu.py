@@ -65,6 +65,13 @@ WORKER = textwrap.dedent(r'''
             e5 = O.max_rel_err(y5, ref * (it + 1))
             assert y5.shape == (M, N) and e5 <= 1e-2, (chunks, it, e5)
         pg.close()
+    # (e) vocab-parallel softmax of the local shards: no logit gather
+    local = lin.forward(a.cuda(), gather=False)
+    sm = S.vocab_parallel_softmax(local, n1 - n0)
+    torch.cuda.synchronize()
+    refp = O.softmax_ref(ref)[:, n0:n1]
+    got = sm.float().cpu().numpy()
+    assert (np.abs(got - refp) <= 1e-2 * np.abs(refp) + 1e-6).all(), "vocab-parallel softmax"
     torch.cuda.synchronize(); comm.close(); dist.destroy_process_group()
     print("rank", rank, "ok", e1, e2, e3, e4)
 ''')
