@@ -80,6 +80,12 @@ struct GemmParams {
   int32_t batch;                  // items (1 = a plain GEMM)
   int32_t batch_tiles;            // m_tiles * n_tiles of one item
   int32_t batch_rows;             // rows of one item (a multiple of kBM)
+  // Implicit-GEMM convolution (conv != 0): A is the NHWC activation through a
+  // 4-D map {C, W, H, N}; output row m is pixel m of NHWC order (tiles of
+  // kBM consecutive pixels = whole rows of the image); K block kb is filter
+  // tap kb / conv_cpb (kh * KW + kw) and channels 64 * (kb % conv_cpb) + [0, 64).
+  int32_t conv;
+  int32_t conv_H, conv_W, conv_KW, conv_cpb, conv_pad_h, conv_pad_w;
   EpiArgs epi;
 };
 
@@ -377,7 +383,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producer
     auto load_a = [&](uint64_t *fb, int stage, int m0, int sb, int b) {
       uint8_t *dstA = sA + stage * A_ST;
-      if (p.batch > 1)
+      if (p.conv) {  // kbs == 1: one filter tap x 64 channels of 128 pixels
+        const int hw = p.conv_H * p.conv_W;
+        const int img = m0 / hw, rem = m0 - img * hw;
+        const int h0 = rem / p.conv_W, w0 = rem - h0 * p.conv_W;
+        const int tap = sb / p.conv_cpb, cb = sb - tap * p.conv_cpb;
+        const int kh = tap / p.conv_KW, kw = tap - kh * p.conv_KW;
+        tma_load_4d(dstA, &tmA, fb, cb * Cfg::kBKElems, w0 + kw - p.conv_pad_w, h0 + kh - p.conv_pad_h, img);
+      } else if (p.batch > 1)
         tma_load_3d(dstA, &tmA, fb, sb * Cfg::kBKElems, m0, b);
       else if (!B_MN && p.use3d)
         tma_load_3d(dstA, &tmA, fb, 0, m0, sb * p.kbs);

@@ -174,6 +174,36 @@ int make_tmap_batched(CUtensorMap *map, const void *ptr, int dtype, uint64_t inn
   return HX_OK;
 }
 
+// 4-D view of NHWC activations for the implicit-GEMM convolution:
+// {C, W, H, N}, box {64 channels (128 bytes), bw, bh, 1}.
+int make_tmap_conv(CUtensorMap *map, const void *ptr, int dtype, uint64_t N, uint64_t H, uint64_t W,
+                   uint64_t C, uint32_t box_c, uint32_t bw, uint32_t bh) {
+  auto enc = get_encode();
+  if (!enc) {
+    g_last_error = "cuTensorMapEncodeTiled unavailable";
+    return HX_E_CUDA;
+  }
+  CUtensorMapDataType dt;
+  switch (dtype) {
+    case HX_F16: dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16; break;
+    case HX_BF16: dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; break;
+    default: return unsupported("convolution dtype");
+  }
+  const uint64_t ez = 2;
+  cuuint64_t dims[4] = {C, W, H, N};
+  cuuint64_t strides[3] = {C * ez, W * C * ez, H * W * C * ez};
+  cuuint32_t box[4] = {box_c, bw, bh, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dt, 4, const_cast<void *>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    g_last_error = "cuTensorMapEncodeTiled (conv) failed (code " + std::to_string(int(r)) + ")";
+    return HX_E_UNSUPPORTED;
+  }
+  return HX_OK;
+}
+
 int esize(int dtype) {
   switch (dtype) {
     case HX_F16:
@@ -449,8 +479,15 @@ struct BatchSpec {
 };
 constexpr int kNeedsLoop = 2;  // internal: the batch is not one launch; run item by item
 
+// The implicit-GEMM convolution's geometry (hx_conv2d): output dims OH x OW,
+// box of bw x bh input pixels per 128-row tile.
+struct ConvSpec {
+  int64_t N, H, W, C, OH, OW, KH, KW;
+  int pad_h, pad_w, bw, bh;
+};
+
 int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = nullptr,
-              const BatchSpec *bt = nullptr, const NormSpec *ns = nullptr) {
+              const BatchSpec *bt = nullptr, const NormSpec *ns = nullptr, const ConvSpec *cv = nullptr) {
   int rc = validate(d);
   if (rc != HX_OK) return rc;
   if (d->M == 0 || d->N == 0) return HX_OK;
@@ -469,6 +506,7 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = 
   // One launch over every batch item when each item's rows are whole tiles
   // and C (and the residual) are items of rows back to back.
   const bool batched = bt != nullptr && bt->count > 1;
+  if (cv && !tma_ok) return unsupported("implicit convolution needs 16-byte aligned operands");
   if (batched) {
     const bool one_launch = tma_ok && !swiglu && peers == nullptr && d->M % kBM == 0 &&
                             bt->sc == d->M * d->ldc && (!d->residual || bt->sr == d->M * d->ldr) &&
@@ -487,7 +525,7 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = 
     plan_tiles(batched ? d->M * bt->count : d->M, d->N, d->K, ez, swiglu, bmn, sms, bn, splits,
                batched ? 1 : d->split_k);
   }
-  if (batched) splits = 1;
+  if (batched || cv) splits = 1;
   if (bn != 64 && bn != 96 && bn != 128 && bn != 192 && bn != 256)
     return arg_fail("tile_n must be 64, 96, 128, 192 or 256");
   if (bmn && ez == 1 && bn < 128) return unsupported("tile_n 64 with int8 B[K,N]");
@@ -495,7 +533,7 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = 
   if ((bn == 96 || bn == 192) && bmn) return unsupported("tile_n 96 / 192 with B[K,N]");
   // Several 128-byte K blocks per TMA instruction when K is whole blocks:
   // the per-instruction cost of TMA, not bytes, limits small boxes.
-  const bool use3d = !batched && !bmn && (d->K * ez) % kKBytes == 0;
+  const bool use3d = !batched && !cv && !bmn && (d->K * ez) % kKBytes == 0;
   // CTA pairs (256 x 256 tiles, cta_group::2) for GEMMs with at least a wave
   // of pair tiles: each SM then ingests 1/3 fewer bytes per flop.
   bool pair = false;
@@ -527,7 +565,12 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = 
   const int out_w = swiglu ? bn / 2 : bn;
 
   CUtensorMap ta, tb;
-  if (batched) {
+  if (cv) {
+    rc = make_tmap_conv(&ta, d->A, d->a_dtype, cv->N, cv->H, cv->W, cv->C, bk, cv->bw, cv->bh);
+    if (rc != HX_OK) return rc;
+    rc = make_tmap(&tb, d->B, d->b_dtype, d->K, d->N, d->ldb, bk, bn);
+    if (rc != HX_OK) return rc;
+  } else if (batched) {
     rc = make_tmap_batched(&ta, d->A, d->a_dtype, d->K, d->M, bt->count, d->lda * ez, bt->sa * ez, bk, kBM);
     if (rc != HX_OK) return rc;
     if (bmn)
@@ -569,6 +612,13 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = 
   p.batch = batched ? static_cast<int32_t>(bt->count) : 1;
   p.batch_tiles = static_cast<int32_t>(item_tiles);
   p.batch_rows = static_cast<int32_t>(d->M);
+  p.conv = cv ? 1 : 0;
+  p.conv_H = cv ? static_cast<int32_t>(cv->OH) : 0;
+  p.conv_W = cv ? static_cast<int32_t>(cv->OW) : 0;
+  p.conv_KW = cv ? static_cast<int32_t>(cv->KW) : 0;
+  p.conv_cpb = cv ? static_cast<int32_t>(cv->C / bk) : 0;
+  p.conv_pad_h = cv ? cv->pad_h : 0;
+  p.conv_pad_w = cv ? cv->pad_w : 0;
   p.total_tiles = static_cast<int32_t>(total);
   p.stages = stages;
   p.kbs = kbs;
@@ -1124,6 +1174,99 @@ int nccl_fail(int r, const char *where) {
 }
 }  // namespace
 
+// ------------------------------------------------------------ convolution
+namespace hx {
+namespace {
+// Explicit im2col for convolutions the implicit GEMM does not take:
+// col[pixel][(kh * KW + kw) * C + c] = x[n][ih][iw][c], zero outside the image.
+// VEC elements (16 bytes or 2) per thread.
+template <int VEC>
+__global__ void im2col_kernel(const uint16_t *x, uint16_t *col, int64_t N, int64_t H, int64_t W, int64_t C,
+                              int64_t OH, int64_t OW, int64_t KH, int64_t KW, int sh, int sw, int ph, int pw,
+                              int dh, int dw) {
+  const int64_t cv = C / VEC;
+  const int64_t total = N * OH * OW * KH * KW * cv;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    int64_t r = i;
+    const int64_t c = (r % cv) * VEC;
+    r /= cv;
+    const int64_t kw = r % KW;
+    r /= KW;
+    const int64_t kh = r % KH;
+    const int64_t pix = r / KH;
+    const int64_t ow = pix % OW, oh = (pix / OW) % OH, n = pix / (OW * OH);
+    const int64_t ih = oh * sh + kh * dh - ph, iw = ow * sw + kw * dw - pw;
+    uint16_t *dst = col + pix * (KH * KW * C) + (kh * KW + kw) * C + c;
+    const bool in = ih >= 0 && ih < H && iw >= 0 && iw < W;
+    if constexpr (VEC == 8) {
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (in) v = *reinterpret_cast<const uint4 *>(x + ((n * H + ih) * W + iw) * C + c);
+      *reinterpret_cast<uint4 *>(dst) = v;
+    } else {
+      dst[0] = in ? x[((n * H + ih) * W + iw) * C + c] : uint16_t(0);
+    }
+  }
+}
+
+struct ConvGeom {
+  int64_t OH, OW, M, K;
+  bool implicit;
+  int bw, bh;
+};
+
+int conv_geom(const hx_conv2d_desc *d, ConvGeom *g) {
+  if (!d) return arg_fail("null descriptor");
+  if (d->N < 0 || d->H <= 0 || d->W <= 0 || d->C <= 0 || d->OC <= 0 || d->KH <= 0 || d->KW <= 0)
+    return arg_fail("convolution sizes");
+  if (d->stride_h <= 0 || d->stride_w <= 0 || d->dil_h <= 0 || d->dil_w <= 0 || d->pad_h < 0 || d->pad_w < 0)
+    return arg_fail("convolution stride / dilation / padding");
+  if (d->dtype != HX_F16 && d->dtype != HX_BF16) return unsupported("convolution takes f16 or bf16");
+  if (d->epilogue == HX_EPI_SWIGLU || d->epilogue == HX_EPI_DEQUANT_SCALE)
+    return unsupported("convolution epilogue");
+  g->OH = (d->H + 2 * d->pad_h - int64_t(d->dil_h) * (d->KH - 1) - 1) / d->stride_h + 1;
+  g->OW = (d->W + 2 * d->pad_w - int64_t(d->dil_w) * (d->KW - 1) - 1) / d->stride_w + 1;
+  if (g->OH <= 0 || g->OW <= 0) return arg_fail("convolution output is empty");
+  g->M = d->N * g->OH * g->OW;
+  g->K = d->KH * d->KW * d->C;
+  if (g->M > INT32_MAX || g->K > INT32_MAX || d->OC > INT32_MAX / 2) return unsupported("size beyond int32 range");
+  const bool rows_tile = (g->OW <= kBM && kBM % g->OW == 0) || g->OW % kBM == 0;
+  g->implicit = d->stride_h == 1 && d->stride_w == 1 && d->dil_h == 1 && d->dil_w == 1 && d->C % 64 == 0 &&
+                rows_tile && (d->N == 1 || (g->OH * g->OW) % kBM == 0) && aligned16(d->x) && aligned16(d->w) &&
+                d->W <= INT32_MAX && d->H <= INT32_MAX;
+  g->bw = static_cast<int>(std::min<int64_t>(g->OW, kBM));
+  g->bh = kBM / g->bw;
+  // every box lies within the image's rows: a tile never needs rows past OH
+  // (images smaller than one 128-pixel tile take the im2col path)
+  if (g->bh > g->OH) g->implicit = false;
+  return HX_OK;
+}
+
+hx_gemm_desc conv_gemm_desc(const hx_conv2d_desc *d, const ConvGeom &g, const void *a) {
+  hx_gemm_desc q;
+  std::memset(&q, 0, sizeof(q));
+  q.M = g.M;
+  q.N = d->OC;
+  q.K = g.K;
+  q.a_dtype = q.b_dtype = q.c_dtype = d->dtype;
+  q.b_layout = HX_B_NK;
+  q.A = a;
+  q.lda = g.K;
+  q.B = d->w;
+  q.ldb = g.K;
+  q.C = d->y;
+  q.ldc = d->OC;
+  q.epilogue = d->epilogue;
+  q.bias = d->bias;
+  q.bias_dtype = d->bias_dtype;
+  q.residual = d->residual;
+  q.ldr = d->OC;
+  q.error_flag = d->error_flag;
+  q.split_k = 1;
+  return q;
+}
+}  // namespace
+}  // namespace hx
+
 // ============================================================ C ABI
 // ------------------------------------------------------------ fused all-gather over NVLink
 namespace hx {
@@ -1243,6 +1386,52 @@ int hx_gemm_batched(const hx_gemm_desc *d, int64_t batch, int64_t stride_a, int6
     if (rc != HX_OK) return rc;
   }
   return HX_OK;
+}
+
+int hx_conv2d_workspace_size(const hx_conv2d_desc *d, int64_t *bytes) {
+  hx::g_last_error.clear();
+  if (!bytes) return HX_E_INVALID_ARG;
+  hx::ConvGeom g;
+  const int rc = hx::conv_geom(d, &g);
+  if (rc != HX_OK) return rc;
+  *bytes = g.implicit ? 0 : (g.M * g.K * 2 + 15) / 16 * 16;
+  return HX_OK;
+}
+
+int hx_conv2d(const hx_conv2d_desc *d, void *workspace, int64_t workspace_bytes, void *stream) {
+  hx::g_last_error.clear();
+  hx::ConvGeom g;
+  int rc = hx::conv_geom(d, &g);
+  if (rc != HX_OK) return rc;
+  if (g.M == 0) return HX_OK;
+  if (!d->x || !d->w || !d->y) return HX_E_INVALID_ARG;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (g.implicit) {
+    hx_gemm_desc q = hx::conv_gemm_desc(d, g, d->x);
+    const hx::ConvSpec cv{d->N, d->H, d->W, d->C, g.OH, g.OW, d->KH, d->KW, d->pad_h, d->pad_w, g.bw, g.bh};
+    return hx::gemm_impl(&q, s, nullptr, nullptr, nullptr, &cv);
+  }
+  const int64_t need = (g.M * g.K * 2 + 15) / 16 * 16;
+  if (!workspace || workspace_bytes < need) {
+    hx::g_last_error = "hx_conv2d needs hx_conv2d_workspace_size() bytes of workspace for this shape";
+    return HX_E_INVALID_ARG;
+  }
+  if (!hx::aligned16(workspace)) return HX_E_INVALID_ARG;
+  const bool v8 = d->C % 8 == 0 && hx::aligned16(d->x);
+  const int64_t items = g.M * d->KH * d->KW * (v8 ? d->C / 8 : d->C);
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((items + 255) / 256, 148 * 16));
+  auto x = static_cast<const uint16_t *>(d->x);
+  auto col = static_cast<uint16_t *>(workspace);
+  if (v8)
+    hx::im2col_kernel<8><<<blocks, 256, 0, s>>>(x, col, d->N, d->H, d->W, d->C, g.OH, g.OW, d->KH, d->KW,
+                                                d->stride_h, d->stride_w, d->pad_h, d->pad_w, d->dil_h, d->dil_w);
+  else
+    hx::im2col_kernel<1><<<blocks, 256, 0, s>>>(x, col, d->N, d->H, d->W, d->C, g.OH, g.OW, d->KH, d->KW,
+                                                d->stride_h, d->stride_w, d->pad_h, d->pad_w, d->dil_h, d->dil_w);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return hx::cuda_fail(e, "im2col_kernel");
+  hx_gemm_desc q = hx::conv_gemm_desc(d, g, workspace);
+  return hx::gemm_impl(&q, s);
 }
 
 int hx_gemm_norm(const hx_gemm_desc *d, int kind, const float *row_stats, const float *col_sum,

@@ -83,6 +83,17 @@ __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *m
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+// 4-D tiled bulk tensor load (x innermost).  The implicit-GEMM convolution
+// reads NHWC activations as {channel, width, height, image}; y / z may be
+// negative or past the edge (the fill value, zero, pads the image).
+__device__ __forceinline__ void tma_load_4d(void *smem_dst, const CUtensorMap *map, uint64_t *bar,
+                                            int32_t x, int32_t y, int32_t z, int32_t w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
 // Same as tma_load_2d, with an L2 eviction-priority hint (createpolicy result).
 __device__ __forceinline__ void tma_load_2d_hint(void *smem_dst, const CUtensorMap *map,
                                                  uint64_t *bar, int32_t x, int32_t y,

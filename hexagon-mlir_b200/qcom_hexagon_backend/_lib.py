@@ -95,6 +95,22 @@ class HxGemmDesc(ctypes.Structure):
     ]
 
 
+class HxConv2dDesc(ctypes.Structure):
+    """Mirror of `hx_conv2d_desc`."""
+
+    _fields_ = [
+        ("N", ctypes.c_int64), ("H", ctypes.c_int64), ("W", ctypes.c_int64), ("C", ctypes.c_int64),
+        ("OC", ctypes.c_int64), ("KH", ctypes.c_int64), ("KW", ctypes.c_int64),
+        ("stride_h", ctypes.c_int32), ("stride_w", ctypes.c_int32),
+        ("pad_h", ctypes.c_int32), ("pad_w", ctypes.c_int32),
+        ("dil_h", ctypes.c_int32), ("dil_w", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("y", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p), ("bias_dtype", ctypes.c_int32), ("epilogue", ctypes.c_int32),
+        ("residual", ctypes.c_void_p), ("error_flag", ctypes.c_void_p),
+    ]
+
+
 class HxW8A16Proj(ctypes.Structure):
     """Mirror of `hx_w8a16_proj`."""
 
@@ -113,6 +129,8 @@ _I64, _I32, _VP = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
 SIGNATURES = {
     "hx_gemm": (_I32, [ctypes.POINTER(HxGemmDesc), _VP]),
     "hx_gemm_batched": (_I32, [ctypes.POINTER(HxGemmDesc), _I64, _I64, _I64, _I64, _I64, _VP]),
+    "hx_conv2d_workspace_size": (_I32, [ctypes.POINTER(HxConv2dDesc), ctypes.POINTER(_I64)]),
+    "hx_conv2d": (_I32, [ctypes.POINTER(HxConv2dDesc), _VP, _I64, _VP]),
     "hx_gemm_norm": (_I32, [ctypes.POINTER(HxGemmDesc), _I32, _VP, _VP, _VP]),
     "hx_softmax": (_I32, [_VP, _I32, _I64, _I64, _I64, _VP, _I32, _I64, _I32, _VP]),
     "hx_softmax_stats": (_I32, [_VP, _I32, _I64, _I64, _I64, _VP, _VP]),

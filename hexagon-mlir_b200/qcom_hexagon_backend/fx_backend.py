@@ -29,6 +29,9 @@ inference-mode dropout, which it re-applies to the fused result:
   linear(x) + r   /   r + linear(x)  -> bias + residual epilogue
   silu(linear_g(x)) * linear_u(x)    -> SwiGLU epilogue over [W_g; W_u]
                                         (both without bias, same x)
+Convolutions (nn.Conv2d / aten.conv2d, groups 1, constant filters) become
+the implicit-GEMM convolution (hx_conv2d), filters permuted once to
+[OC, KH, KW, C]: the conv consumer of HMX in MatmulToConvPass.cpp.
 Batched products (torch.bmm / aten.bmm, and matmul with both operands of
 rank >= 3, e.g. attention's q @ k^T and p @ v) become one batched GEMM
 (hx_bmm), the batch_matmul / batch_matmul_transpose_b of
@@ -107,6 +110,16 @@ def hx_bmm(x, y):
     y is a transposed view."""
     ops.chain_flush()
     return ops.matmul_batched(x, y)
+
+
+def hx_conv2d(x, weight_ohwi, bias, stride, padding, dilation):
+    """nn.Conv2d / aten.conv2d (groups 1) as the implicit-GEMM convolution:
+    NCHW in and out, computed channels-last with the filters pre-permuted to
+    [OC, KH, KW, C] once at compile time."""
+    ops.chain_flush()
+    y = ops.conv2d_nhwc(x.permute(0, 2, 3, 1), weight_ohwi, bias, stride=stride, padding=padding,
+                        dilation=dilation)
+    return y.permute(0, 3, 1, 2)
 
 
 def hx_swiglu(x, weight_gate_up, norm_kind=None, norm_stats=None, col_sum=None):
@@ -432,6 +445,7 @@ def rewrite(gm: fx.GraphModule) -> fx.GraphModule:
             graph.erase_node(dead)
         graph.erase_node(n)
     _rewrite_batched(gm)
+    _rewrite_convs(gm)
     _fold_norms(gm)
     graph.lint()
     gm.recompile()
@@ -565,6 +579,56 @@ def _fold_norms(gm: fx.GraphModule) -> None:
         graph.erase_node(n)
 
 
+_CONV_FNS = (F.conv2d, aten.conv2d.default)
+
+
+def _rewrite_convs(gm: fx.GraphModule) -> None:
+    """Conv2d with constant filters, groups 1, numeric padding -> hx_conv2d."""
+    graph = gm.graph
+    done = {}
+    for n in list(graph.nodes):
+        if n.op == "call_module":
+            mod = gm.get_submodule(n.target)
+            if not (isinstance(mod, nn.Conv2d) and mod.groups == 1 and not isinstance(mod.padding, str)
+                    and mod.padding_mode == "zeros" and len(n.args) == 1 and not n.kwargs):
+                continue
+            x, wname = n.args[0], n.target + ".weight"
+            bname = n.target + ".bias" if mod.bias is not None else None
+            stride, padding, dilation = tuple(mod.stride), tuple(mod.padding), tuple(mod.dilation)
+        elif n.op == "call_function" and n.target in _CONV_FNS:
+            args = list(n.args) + [None] * (7 - len(n.args))
+            names = ["input", "weight", "bias", "stride", "padding", "dilation", "groups"]
+            vals = {k: n.kwargs.get(k, a) for k, a in zip(names, args)}
+            w, b = vals["weight"], vals["bias"]
+            groups = vals["groups"] if vals["groups"] is not None else 1
+            if groups != 1 or isinstance(vals["padding"], str):
+                continue
+            if not (isinstance(w, fx.Node) and w.op == "get_attr"):
+                continue
+            if b is not None and not (isinstance(b, fx.Node) and b.op == "get_attr"):
+                continue
+            x, wname, bname = vals["input"], w.target, (b.target if b is not None else None)
+            pr = lambda v, d: tuple(v) if isinstance(v, (list, tuple)) else ((v, v) if v is not None else (d, d))
+            stride, padding, dilation = pr(vals["stride"], 1), pr(vals["padding"], 0), pr(vals["dilation"], 1)
+            if len(stride) != 2 or len(padding) != 2 or len(dilation) != 2:
+                continue
+        else:
+            continue
+        weight = _get_attr(gm, wname)
+        if not isinstance(weight, torch.Tensor) or weight.dim() != 4:
+            continue
+        if wname not in done:
+            name = f"_hx_conv_w{len(done)}"
+            gm.register_buffer(name, weight.detach().permute(0, 2, 3, 1).contiguous())
+            done[wname] = name
+        with graph.inserting_before(n):
+            wnode = graph.get_attr(done[wname])
+            bnode = graph.get_attr(bname) if bname else None
+            new = graph.call_function(hx_conv2d, (x, wnode, bnode, stride, padding, dilation))
+        n.replace_all_uses_with(new)
+        graph.erase_node(n)
+
+
 def _rewrite_batched(gm: fx.GraphModule) -> None:
     """bmm / matmul nodes whose operands are both batched (rank >= 3 known
     from export metadata, or bmm itself) -> hx_bmm."""
@@ -595,7 +659,8 @@ def insert_chain_flushes(gm: fx.GraphModule) -> fx.GraphModule:
     for n in list(graph.nodes):
         if n.op in ("placeholder", "get_attr"):
             continue
-        if n.op == "call_function" and (n.target in (hx_linear, hx_swiglu, hx_bmm, hx_norm_stats, ops.chain_flush)
+        if n.op == "call_function" and (n.target in (hx_linear, hx_swiglu, hx_bmm, hx_conv2d, hx_norm_stats,
+                                                     ops.chain_flush)
                                         or n.target is operator.getitem):
             continue
         with graph.inserting_before(n):
@@ -607,7 +672,7 @@ def insert_chain_flushes(gm: fx.GraphModule) -> fx.GraphModule:
 
 def count_hx_calls(gm: fx.GraphModule) -> int:
     return sum(1 for n in gm.graph.nodes
-               if n.op == "call_function" and n.target in (hx_linear, hx_swiglu, hx_bmm))
+               if n.op == "call_function" and n.target in (hx_linear, hx_swiglu, hx_bmm, hx_conv2d))
 
 
 def capture(module: nn.Module, example_inputs=None, mode: str = "auto") -> fx.GraphModule:

@@ -371,6 +371,76 @@ def matmul(a: torch.Tensor, b: torch.Tensor, *, out: Optional[torch.Tensor] = No
     return gemm(a, b, b_layout="kn", out=out, out_dtype=out_dtype, **kw)
 
 
+def _pair(v):
+    return (v, v) if isinstance(v, int) else tuple(v)
+
+
+def conv2d_nhwc(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None, *, stride=1, padding=0,
+                dilation=1, epilogue: Optional[str] = None, residual: Optional[torch.Tensor] = None,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """2-D convolution as a GEMM (hx_conv2d): x [N, H, W, C] (channels
+    innermost), w [OC, KH, KW, C]; returns y [N, OH, OW, OC].  epilogue
+    defaults to "bias" with a bias, else "none"; "bias_gelu_tanh",
+    "bias_silu", "residual", "bias_residual" are fused too.  The im2col
+    workspace, when the shape needs one, is allocated here on x's device."""
+    _check_cuda(x, "x")
+    _check_cuda(w, "w", x.device)
+    if x.dim() != 4 or w.dim() != 4 or x.shape[3] != w.shape[3]:
+        raise ValueError(f"x must be [N,H,W,C] and w [OC,KH,KW,C], got {tuple(x.shape)} and {tuple(w.shape)}")
+    if x.dtype != w.dtype or x.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("conv2d takes f16 or bf16 x and w of the same dtype")
+    x = x.contiguous()
+    w = w.contiguous()
+    (sh, sw), (ph, pw), (dh, dw) = _pair(stride), _pair(padding), _pair(dilation)
+    N, H, W, C = x.shape
+    OC, KH, KW, _ = w.shape
+    OH = (H + 2 * ph - dh * (KH - 1) - 1) // sh + 1
+    OW = (W + 2 * pw - dw * (KW - 1) - 1) // sw + 1
+    if epilogue is None:
+        epilogue = "bias" if bias is not None else "none"
+    if out is None:
+        out = torch.empty((N, OH, OW, OC), dtype=x.dtype, device=x.device)
+    d = _lib.HxConv2dDesc()
+    d.N, d.H, d.W, d.C, d.OC, d.KH, d.KW = N, H, W, C, OC, KH, KW
+    d.stride_h, d.stride_w, d.pad_h, d.pad_w, d.dil_h, d.dil_w = sh, sw, ph, pw, dh, dw
+    d.dtype = _dtype_code(x, "x")
+    d.x, d.w, d.y = x.data_ptr(), w.data_ptr(), out.data_ptr()
+    if bias is not None:
+        _check_cuda(bias, "bias", x.device)
+        bias = bias.contiguous()
+        d.bias, d.bias_dtype = bias.data_ptr(), _dtype_code(bias, "bias")
+    d.epilogue = _lib.EPILOGUES[epilogue]
+    if residual is not None:
+        _check_cuda(residual, "residual", x.device)
+        if tuple(residual.shape) != tuple(out.shape) or not residual.is_contiguous() or residual.dtype != out.dtype:
+            raise ValueError("residual must be a contiguous [N, OH, OW, OC] tensor of y's dtype")
+        d.residual = residual.data_ptr()
+    lib = _lib.load()
+    nbytes = ctypes.c_int64()
+    _lib.check(lib.hx_conv2d_workspace_size(ctypes.byref(d), ctypes.byref(nbytes)), "hx_conv2d_workspace_size")
+    ws = torch.empty(max(nbytes.value, 1), dtype=torch.uint8, device=x.device) if nbytes.value else None
+    with torch.cuda.device(x.device):
+        rc = lib.hx_conv2d(ctypes.byref(d), ctypes.c_void_p(ws.data_ptr() if ws is not None else 0), nbytes.value,
+                           ctypes.c_void_p(_stream_ptr(x.device)))
+    _lib.check(rc, "hx_conv2d")
+    return out
+
+
+def conv2d(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None, stride=1, padding=0,
+           dilation=1, groups: int = 1) -> torch.Tensor:
+    """F.conv2d on NCHW tensors (groups == 1) through conv2d_nhwc: x is read
+    as channels-last (no copy when x is already torch.channels_last) and the
+    result is returned as an NCHW-shaped channels-last tensor."""
+    if groups != 1:
+        raise ValueError("conv2d: groups must be 1")
+    if isinstance(padding, str):
+        raise ValueError("conv2d: string padding is not supported")
+    x_nhwc = x.permute(0, 2, 3, 1)
+    w_ohwi = weight.permute(0, 2, 3, 1)
+    y = conv2d_nhwc(x_nhwc, w_ohwi, bias, stride=stride, padding=padding, dilation=dilation)
+    return y.permute(0, 3, 1, 2)
+
+
 _NORM_KINDS = {"layer": _lib.HX_NORM_LAYER, "rms": _lib.HX_NORM_RMS}
 
 

@@ -268,6 +268,39 @@ int hx_sharded_gemm_gather_p2p(const hx_gemm_desc *d, int rank, int world, void 
 int hx_gemm_batched(const hx_gemm_desc *d, int64_t batch, int64_t stride_a, int64_t stride_b,
                     int64_t stride_c, int64_t stride_r, void *stream);
 
+/* ---- convolution as an implicit GEMM ----------------------------------- */
+
+/* 2-D convolution, NHWC activations and OHWI filters (channels innermost):
+     y[n, oh, ow, o] = epilogue( sum_{kh, kw, c} x[n, oh*sh + kh*dh - ph, ow*sw + kw*dw - pw, c]
+                                                 * w[o, kh, kw, c] )
+   with zero padding.  As a GEMM: M = N*OH*OW output pixels, N = OC,
+   K = KH*KW*C, B = w as W[OC, KH*KW*C].  Reference: MatmulToConvPass.cpp
+   (the reverse mapping, matmul -> conv_2d_nhwc_fhwc) and the HMX conv path
+   exercised by benchmark_models/micro_bench/test_conv_benchmark.py. */
+typedef struct hx_conv2d_desc {
+  int64_t N, H, W, C;        /* input [N, H, W, C]                             */
+  int64_t OC, KH, KW;        /* filters [OC, KH, KW, C]                        */
+  int32_t stride_h, stride_w, pad_h, pad_w, dil_h, dil_w;
+  int32_t dtype;             /* HX_F16 or HX_BF16, for x, w and y              */
+  const void *x;
+  const void *w;
+  void *y;                   /* [N, OH, OW, OC], OH = (H + 2ph - dh(KH-1) - 1)/sh + 1 */
+  const void *bias;          /* [OC] or NULL                                   */
+  int32_t bias_dtype;
+  int32_t epilogue;          /* HX_EPI_* except SWIGLU / DEQUANT_SCALE         */
+  const void *residual;      /* [N, OH, OW, OC] for the residual epilogues     */
+  int32_t *error_flag;       /* optional, as in hx_gemm_desc                   */
+} hx_conv2d_desc;
+
+/* Bytes of workspace hx_conv2d needs.  0 for the implicit GEMM (stride 1,
+   dilation 1, C a multiple of 64, output rows that tile 128-pixel blocks:
+   OW divides 128 or is a multiple of it, 128 / OW <= OH, and N == 1 or OH*OW
+   a multiple of 128): each K block is then one filter tap x 64 channels, loaded by a 4-D
+   TMA box at the tap-shifted coordinates, whose zero fill is the padding.
+   Otherwise M * K elements for an explicit im2col matrix. */
+int hx_conv2d_workspace_size(const hx_conv2d_desc *d, int64_t *bytes);
+int hx_conv2d(const hx_conv2d_desc *d, void *workspace, int64_t workspace_bytes, void *stream);
+
 /* ---- row kernels either side of the linear layer ---------------------- */
 
 /* Softmax over rows of x[M, N] (dtype HX_F16 / HX_BF16 / HX_F32, row stride

@@ -173,3 +173,29 @@ def norm_linear_ref(x, w, *, kind="layer", gamma=None, beta=None, eps=1e-5, epil
     fp32 linear oracle.  (Unfused reference order: norm pass, then matmul.)"""
     y = norm_ref(x, kind, gamma, beta, eps).astype(np.float32)
     return linear_ref(y, w, epilogue=epilogue, bias=bias, residual=residual)
+
+
+def conv2d_nhwc_ref(x, w, *, stride=(1, 1), padding=(0, 0), dilation=(1, 1), bias=None) -> np.ndarray:
+    """fp32 2-D convolution of upcast operands, NHWC activations and OHWI
+    filters, zero padding: the golden of
+    benchmark_models/micro_bench/test_conv_benchmark.py (torch nn.Conv2d on
+    the CPU), written as a sum over filter taps of [pixels, C] @ [C, OC]."""
+    X = as_f32(x)
+    Wt = as_f32(w)
+    N, H, W, C = X.shape
+    OC, KH, KW, _ = Wt.shape
+    sh, sw = stride
+    ph, pw = padding
+    dh, dw = dilation
+    OH = (H + 2 * ph - dh * (KH - 1) - 1) // sh + 1
+    OW = (W + 2 * pw - dw * (KW - 1) - 1) // sw + 1
+    Xp = np.zeros((N, H + 2 * ph, W + 2 * pw, C), np.float32)
+    Xp[:, ph:ph + H, pw:pw + W, :] = X
+    out = np.zeros((N, OH, OW, OC), np.float32)
+    for kh in range(KH):
+        for kw in range(KW):
+            patch = Xp[:, kh * dh: kh * dh + (OH - 1) * sh + 1: sh, kw * dw: kw * dw + (OW - 1) * sw + 1: sw, :]
+            out += (patch.reshape(-1, C) @ Wt[:, kh, kw, :].T).reshape(N, OH, OW, OC)
+    if bias is not None:
+        out += as_f32(bias)
+    return out

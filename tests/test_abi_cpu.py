@@ -41,21 +41,23 @@ def test_ctypes_table_covers_header():
     assert set(header_functions()) <= set(_lib.SIGNATURES)
 
 
-def test_desc_layout_matches_c(tmp_path):
-    """sizeof/offsetof of hx_gemm_desc from the C compiler == the ctypes mirror."""
-    fields = [f for f, _ in _lib.HxGemmDesc._fields_]
+@pytest.mark.parametrize("cname,cls", [("hx_gemm_desc", _lib.HxGemmDesc), ("hx_conv2d_desc", _lib.HxConv2dDesc),
+                                       ("hx_w8a16_proj", _lib.HxW8A16Proj)])
+def test_desc_layout_matches_c(tmp_path, cname, cls):
+    """sizeof/offsetof of each C descriptor from the C compiler == the ctypes mirror."""
+    fields = [f for f, _ in cls._fields_]
     prog = ["#include <stdio.h>", "#include <stddef.h>", '#include "hx_gemm.h"', "int main(void){",
-            'printf("%zu\\n", sizeof(hx_gemm_desc));']
-    prog += [f'printf("%zu\\n", offsetof(hx_gemm_desc, {f}));' for f in fields]
+            f'printf("%zu\\n", sizeof({cname}));']
+    prog += [f'printf("%zu\\n", offsetof({cname}, {f}));' for f in fields]
     prog += ["return 0;}"]
     c = tmp_path / "layout.c"
     c.write_text("\n".join(prog))
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(c), "-o", str(exe)], check=True)
     vals = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
-    assert vals[0] == ctypes.sizeof(_lib.HxGemmDesc)
+    assert vals[0] == ctypes.sizeof(cls)
     for f, off in zip(fields, vals[1:]):
-        assert getattr(_lib.HxGemmDesc, f).offset == off, f
+        assert getattr(cls, f).offset == off, f
 
 
 def test_status_strings():

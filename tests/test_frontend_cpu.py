@@ -393,3 +393,25 @@ def test_norm_with_other_user_not_folded():
 
     gm = FX.rewrite(fx.symbolic_trace(M()))
     assert not any(n.target is FX.hx_norm_stats for n in gm.graph.nodes)
+
+
+@pytest.mark.parametrize("mode", ["trace", "export"])
+def test_rewrite_conv2d(mode):
+    class Net(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.c1 = nn.Conv2d(8, 16, 3, padding=1)
+            self.c2 = nn.Conv2d(16, 4, 3, stride=2, bias=False)
+
+        def forward(self, x):
+            return self.c2(F.relu(self.c1(x)))
+
+    m = Net().eval()
+    x = torch.randn(2, 8, 9, 9)
+    gm = FX.rewrite(FX.capture(m, [x], mode))
+    convs = [n for n in gm.graph.nodes if n.op == "call_function" and n.target is FX.hx_conv2d]
+    assert len(convs) == 2
+    for n in convs:  # torch stand-in with the same argument meaning
+        n.target = lambda x, w, b, s, p, d: F.conv2d(x, w.permute(0, 3, 1, 2), b, s, p, d)
+    gm.recompile()
+    torch.testing.assert_close(gm(x), m(x), rtol=1e-5, atol=1e-5)
