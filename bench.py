@@ -1,7 +1,7 @@
 """Benchmark of the B200 linear-layer GEMM path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl hx|reference]
-                    [--workload lmhead|gpt2|qwen|tinyllama] [--lm-dtype bf16|int8]
+                    [--workload lmhead|gpt2|qwen|tinyllama|attn|conv|softmax] [--lm-dtype bf16|int8]
 
 Default workload, at every N (the configuration the headline metric is
 quoted on at 1/2/4/8 GPUs): the LM-head GEMM, bf16, M=16384 tokens x
@@ -235,6 +235,8 @@ def run_hx(args):
         return run_lmhead(args, world, rank, dev, peaks, peak_src)
     if args.workload == "tinyllama":
         return run_tinyllama(args, world, rank, dev, peaks, peak_src)
+    if args.workload in ("attn", "conv", "softmax"):
+        return run_kernel_bench(args, world, rank, dev, peaks, peak_src)
     W = build_gpt2(dev) if args.workload == "gpt2" else build_qwen(dev)
     cg = W["cg"]
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
@@ -598,6 +600,136 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
         dist.destroy_process_group()
 
 
+def run_kernel_bench(args, world, rank, dev, peaks, peak_src):
+    """The rows beside the linear layer, each one step = one call on resident
+    inputs, timed with CUDA events (256 MB L2 flush before each step):
+      attn     batched GEMMs of GPT-2 attention, batch 8 x 12 heads x S 1024 x
+               head 64, fp16: scores q @ k^T (k a transposed view) and context
+               p @ v (hx_gemm_batched); HBM-bound on the 201 MB score matrix;
+      conv     3x3 convolution, NHWC fp16, batch 8 x 64 x 64 x 256 -> 256,
+               padding 1, as an implicit GEMM (hx_conv2d): tensor-bound;
+      softmax  softmax over the 50304-wide vocabulary of the LM head's
+               16384 rows, bf16 in place (hx_softmax): HBM-bound.
+    Independent replicas at N > 1 (weak scaling)."""
+    from qcom_hexagon_backend import ops
+
+    g = torch.Generator().manual_seed(1240)
+    wl = args.workload
+    if wl == "attn":
+        B, Hh, S, D = 8, 12, 1024, 64
+        q_h = torch.randn(B, Hh, S, D, generator=g).half()
+        k_h = torch.randn(B, Hh, S, D, generator=g).half()
+        v_h = torch.randn(B, Hh, S, D, generator=g).half()
+        host_in = [q_h, k_h, v_h]
+        q, k, v = (t.to(dev) for t in host_in)
+        p = torch.empty(B, Hh, S, S, dtype=torch.float16, device=dev)
+        ctx = torch.empty(B, Hh, S, D, dtype=torch.float16, device=dev)
+
+        def step():
+            ops.bmm(q.view(-1, S, D), k.view(-1, S, D), b_layout="nk", out=p.view(-1, S, S))
+            ops.bmm(p.view(-1, S, S), v.view(-1, S, D), b_layout="kn", out=ctx.view(-1, S, D))
+
+        outs = [ctx]
+        work = 2 * (2.0 * B * Hh * S * S * D)
+        nbytes = 2.0 * (4 * B * Hh * S * D + 2 * B * Hh * S * S)  # q,k,v,ctx + scores written and read
+        launches, bound, kern = 2, "hbm", "hx_gemm_sm100_kernel (batched)"
+        cfg = {"workload": "GPT-2 attention batched GEMMs (q@k^T, p@v), fp16", "batch": B, "heads": Hh,
+               "seq_len": S, "head_dim": D}
+        metric, unit = "batched GEMM TFLOP/s", "TFLOP/s"
+    elif wl == "conv":
+        N_, H, W, C, OC = 8, 64, 64, 256, 256
+        x_h = torch.randn(N_, H, W, C, generator=g).half()
+        w_h = (torch.randn(OC, 3, 3, C, generator=g) * 0.02).half()
+        host_in = [x_h]
+        x, w = x_h.to(dev), w_h.to(dev)
+        y = torch.empty(N_, H, W, OC, dtype=torch.float16, device=dev)
+
+        def step():
+            ops.conv2d_nhwc(x, w, None, padding=1, out=y)
+
+        outs = [y]
+        work = 2.0 * N_ * H * W * OC * 9 * C
+        nbytes = 2.0 * (x.numel() + w.numel() + y.numel())
+        launches, bound, kern = 1, "tensor", "hx_gemm_sm100_kernel (implicit conv)"
+        cfg = {"workload": "3x3 conv NHWC fp16 as implicit GEMM", "batch": N_, "H": H, "W": W, "C": C, "OC": OC}
+        metric, unit = "conv TFLOP/s", "TFLOP/s"
+    else:  # softmax
+        M, N = WL.LMHEAD_M, WL.LMHEAD_N
+        x_h = (torch.randn(M, N, generator=g) * 2).to(torch.bfloat16)
+        host_in = [x_h]
+        x = x_h.to(dev)
+
+        def step():
+            ops.softmax(x, out=x)
+
+        outs = [x]
+        nbytes = 2.0 * 2 * M * N
+        work = nbytes
+        launches, bound, kern = 1, "hbm", "softmax_rows_kernel"
+        cfg = {"workload": "LM-head vocabulary softmax, bf16 in place", "M": M, "N": N}
+        metric, unit = "softmax HBM GB/s", "GB/s"
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        step()
+    barrier(world, dev)
+    stream = torch.cuda.current_stream(dev)
+    clk = ClockSampler(dev.index)
+    clk.start()
+    evs = []
+    for _ in range(args.steps):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        step()
+        e.record(stream)
+        evs.append((s, e))
+    barrier(world, dev)
+    clocks = clk.stop()
+    local_ms = sum(s.elapsed_time(e) for s, e in evs) / args.steps
+    ms = max_over_ranks(local_ms, world, dev)
+    if bound == "tensor":
+        rate = work / (ms / 1e3) / 1e12
+        achieved, peak, runit = work / (local_ms / 1e3) / 1e12, float(peaks.get("bf16_tflops", 1590.0)), "TFLOP/s"
+    else:
+        achieved, peak, runit = nbytes / (local_ms / 1e3) / 1e9, float(peaks.get("hbm_gbs", 6650.0)), "GB/s"
+        rate = (work / (ms / 1e3) / 1e12) if unit == "TFLOP/s" else nbytes / (ms / 1e3) / 1e9
+    # e2e: inputs from pinned host memory, the step, outputs back to pinned host memory
+    pin_in = [t.pin_memory() for t in host_in]
+    dev_in = {"attn": lambda: [q, k, v], "conv": lambda: [x], "softmax": lambda: [x]}[wl]()
+    pin_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
+    e2e_ms = []
+    for _ in range(max(3, min(args.steps, 10))):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for d_, h_ in zip(dev_in, pin_in):
+            d_.copy_(h_, non_blocking=True)
+        step()
+        for h_, o_ in zip(pin_out, outs):
+            h_.copy_(o_, non_blocking=True)
+        e.record(stream)
+        e.synchronize()
+        e2e_ms.append(s.elapsed_time(e))
+    e2e_t = max_over_ranks(sum(e2e_ms) / len(e2e_ms), world, dev)
+    e2e_v = (work / (e2e_t / 1e3) / 1e12) if unit == "TFLOP/s" else nbytes / (e2e_t / 1e3) / 1e9
+    line = {"metric": metric, "value": round(rate * world, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16" if wl == "softmax" else "fp16", "data": "synthetic (seeded N(0,1))",
+            "config": dict(cfg, parallelism=f"replicas{world}", l2="flushed (256 MB write) before every timed step"),
+            "e2e": {"value": round(e2e_v * world, 2), "unit": unit,
+                    "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in pin_in),
+                    "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in pin_out)},
+            "gpu_launches": launches * args.steps,
+            "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": runit,
+                         "frac": round(achieved / peak, 4), "traffic": None, "kernel": kern,
+                         "algorithmic_bytes": nbytes,
+                         "peak_source": f"{peak_src} " + ("bf16_tflops (burst)" if bound == "tensor" else "hbm_gbs")},
+            "clocks": clocks}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def run_reference(args):
     """The reference's own CPU path on this box's host cores (rank 0 only)."""
     rank = int(os.environ.get("RANK", "0"))
@@ -628,7 +760,8 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["hx", "reference"], default="hx")
-    ap.add_argument("--workload", choices=["gpt2", "qwen", "tinyllama", "lmhead"], default="lmhead")
+    ap.add_argument("--workload", choices=["gpt2", "qwen", "tinyllama", "lmhead", "attn", "conv", "softmax"],
+                    default="lmhead")
     ap.add_argument("--batch", type=int, default=1, help="decode batch M for --workload tinyllama")
     ap.add_argument("--layers", type=int, default=22, help="decoder layers for --workload tinyllama")
     ap.add_argument("--chain", action="store_true",

@@ -127,7 +127,45 @@ def _lmhead(budget_s, int8=False):
                 config={"workload": f"LM head 16384x2048x50304 {dt}, column-sharded (BASELINE config 5)"})
 
 
-_TABLE = {"gpt2": _gpt2, "qwen": _qwen, "tinyllama": _tinyllama, "lmhead": _lmhead,
+def _attn(budget_s):
+    B, H, S, D = 1, 12, 1024, 64  # one of the GPU arm's 8 sequences, scaled
+    g = torch.Generator().manual_seed(1240)
+    q, k, v = (torch.randn(B, H, S, D, generator=g).half() for _ in range(3))
+    with torch.no_grad():
+        t = _timeit(lambda: torch.matmul(torch.matmul(q, k.transpose(-1, -2)), v), 3)
+    flops = 2 * (2.0 * B * H * S * S * D)
+    return dict(metric="batched GEMM TFLOP/s", unit="TFLOP/s", dtype="fp16", value=round(flops / t / 1e12, 4),
+                ms_per_step=round(t * 1e3 * 8, 3),
+                sample="PyTorch-CPU fp16 q@k^T and p@v for 1 of 8 sequences (12 heads x 1024 x 64), median of 3",
+                config={"workload": "GPT-2 attention batched GEMMs (q@k^T, p@v), fp16"})
+
+
+def _conv(budget_s):
+    g = torch.Generator().manual_seed(1240)
+    x = torch.randn(1, 256, 64, 64, generator=g).half()  # 1 of the GPU arm's 8 images
+    w = (torch.randn(256, 256, 3, 3, generator=g) * 0.02).half()
+    with torch.no_grad():
+        t = _timeit(lambda: F.conv2d(x, w, padding=1), 3)
+    flops = 2.0 * 64 * 64 * 256 * 9 * 256
+    return dict(metric="conv TFLOP/s", unit="TFLOP/s", dtype="fp16", value=round(flops / t / 1e12, 4),
+                ms_per_step=round(t * 1e3 * 8, 3),
+                sample="PyTorch-CPU fp16 F.conv2d 3x3 256->256 on 1 of 8 64x64 images, median of 3",
+                config={"workload": "3x3 conv NHWC fp16 as implicit GEMM"})
+
+
+def _softmax(budget_s):
+    rows = 512
+    g = torch.Generator().manual_seed(1240)
+    x = (torch.randn(rows, WL.LMHEAD_N, generator=g) * 2).to(torch.bfloat16)
+    t = _timeit(lambda: torch.softmax(x, -1), 3)
+    nbytes = 2.0 * 2 * rows * WL.LMHEAD_N
+    return dict(metric="softmax HBM GB/s", unit="GB/s", dtype="bf16", value=round(nbytes / t / 1e9, 3),
+                ms_per_step=round(t * 1e3 * WL.LMHEAD_M / rows, 3),
+                sample=f"PyTorch-CPU bf16 softmax of {rows} of 16384 vocabulary rows, median of 3, scaled",
+                config={"workload": "LM-head vocabulary softmax, bf16 in place"})
+
+
+_TABLE = {"attn": _attn, "conv": _conv, "softmax": _softmax, "gpt2": _gpt2, "qwen": _qwen, "tinyllama": _tinyllama, "lmhead": _lmhead,
           "lmhead_int8": lambda b: _lmhead(b, int8=True)}
 
 

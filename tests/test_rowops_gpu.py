@@ -10,9 +10,10 @@
     (hx_gemm_norm), with bias, GELU, residual and SwiGLU epilogues.
 
 Tolerances: softmax probabilities |y - ref| <= 2e-3 * max(ref) + the output
-dtype's rounding (fp16 / bf16 / fp32 outputs), log-softmax <= 2e-2 absolute
-for 16-bit outputs; normalised linears max rel err <= 1e-2 as every other
-fp16 / bf16 GEMM test.  Reference goldens: test/python/triton/test_softmax.py,
+dtype's rounding (fp16 / bf16 / fp32 outputs), log-softmax <= 1e-4 absolute
+for fp32 outputs; normalised linears max rel err <= 1e-2 as every other
+fp16 / bf16 GEMM test, and a max abs error within 1.5x that of the unfused
+pipeline in the same dtype (normalised activation rounded, then the GEMM).  Reference goldens: test/python/triton/test_softmax.py,
 test_online_softmax.py (atol 1e-5 on fp32 128x128), test_layer_norm.py,
 test_rms_norm.py.
 """
@@ -160,4 +161,14 @@ def test_gemm_with_folded_norm(cuda_device, kind, epilogue, dtype, shape):
                             beta=to_np32(beta) if beta is not None else None, epilogue=epilogue,
                             bias=to_np32(bias) if bias is not None else None,
                             residual=to_np32(res) if res is not None else None)
-    assert_close(to_np32(out), ref)
+    got = to_np32(out)
+    assert O.max_rel_err(got, ref) <= 1e-2
+    # Folding may not cost accuracy against the unfused pipeline in the same
+    # dtype (the normalised activation rounded to it, then the same GEMM).
+    xn = O.norm_ref(to_np32(x), kind, to_np32(gamma), to_np32(beta) if beta is not None else None)
+    unfused = q.gemm(torch.from_numpy(xn.astype(np.float32)).to(dtype).to(d), w.to(d), epilogue=epilogue,
+                     bias=bias.to(d) if bias is not None else None, residual=res.to(d) if res is not None else None)
+    torch.cuda.synchronize()
+    e_fused = np.abs(got - ref).max()
+    e_unfused = np.abs(to_np32(unfused) - ref).max()
+    assert e_fused <= 1.5 * e_unfused + 1e-3 * np.abs(ref).max(), (e_fused, e_unfused)
