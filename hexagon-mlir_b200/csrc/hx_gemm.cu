@@ -605,7 +605,17 @@ int gemm_impl(const hx_gemm_desc *d, cudaStream_t s, const PeerTargets *peers = 
   p.n_tiles = static_cast<int32_t>((d->N + out_w - 1) / out_w);
   p.k_blocks = static_cast<int32_t>((d->K + bk - 1) / bk);
   p.n_half = static_cast<int32_t>(d->N);
-  p.group_m = std::min<int32_t>(16, p.m_tiles);
+  // Grouped raster: 16 row blocks per group, so a group's A panel stays in L2
+  // while it sweeps every column block and each B tile is fetched once per
+  // group.  Larger groups, which would fetch B once in all, measured slower
+  // on the LM head: with 64 row blocks (a 67 MB A panel) the streamed C
+  // writes evict A from L2 and DRAM reads rose from 0.89 to 3.3 GB a launch.
+  {
+    int64_t gm = 16;
+    if (const char *env = std::getenv("HX_GEMM_GROUP_M"))  // tuning switch
+      gm = std::max(1, std::atoi(env));
+    p.group_m = static_cast<int32_t>(std::min<int64_t>(gm, p.m_tiles));
+  }
   const int64_t item_tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
   const int64_t total = item_tiles * (batched ? bt->count : 1);
   if (total > INT32_MAX) return unsupported("too many tiles");

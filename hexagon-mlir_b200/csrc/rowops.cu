@@ -14,7 +14,7 @@
 //     test/python/triton/test_layer_norm.py and test_rms_norm.py define them.
 //
 // All are HBM-bound streaming kernels: one CTA per row (grid-stride over rows,
-// a few CTAs per SM), 16-byte loads where rows are aligned, fp32 arithmetic.
+// up to four 512-thread CTAs per SM), 16-byte loads where rows are aligned, fp32 arithmetic.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -30,7 +30,7 @@
 namespace hx {
 namespace {
 
-constexpr int kRowThreads = 256;
+constexpr int kRowThreads = 512;
 
 template <typename T>
 __device__ __forceinline__ float to_f(T v);
@@ -176,15 +176,36 @@ __global__ void __launch_bounds__(kRowThreads) softmax_apply_kernel(const T *x, 
   }
 }
 
+// VT = 16 / sizeof(T) outputs from VT inputs: one 16-byte store per VT * 2
+// bytes of 16-bit U (two for float U) when the output row is aligned.
+template <typename T, typename U>
+__device__ __forceinline__ void store_outs(U *dst, const float (&o)[16 / sizeof(T)], bool yvec) {
+  constexpr int VT = 16 / sizeof(T);
+  if (yvec && (VT * sizeof(U)) % 16 == 0) {
+    U pk[VT];
+#pragma unroll
+    for (int q = 0; q < VT; ++q) pk[q] = from_f<U>(o[q]);
+#pragma unroll
+    for (int q = 0; q < int(VT * sizeof(U) / 16); ++q)
+      reinterpret_cast<uint4 *>(dst)[q] = reinterpret_cast<const uint4 *>(pk)[q];
+  } else {
+#pragma unroll
+    for (int q = 0; q < VT; ++q) dst[q] = from_f<U>(o[q]);
+  }
+}
+
 // Whole softmax of a row in one CTA: the row is read once and kept in shared
-// memory (in its own dtype) when it fits in kSmemRow bytes, else read twice.
-constexpr int kSmemRow = 200 * 1024;
+// memory (in its own dtype) when it fits in kSmemRow bytes, small enough for
+// two CTAs per SM, else read twice.
+constexpr int kSmemRow = 112 * 1024;
 template <typename T, typename U>
 __global__ void __launch_bounds__(kRowThreads) softmax_rows_kernel(const T *x, int64_t M, int64_t N, int64_t ldx,
-                                                                   bool vec, U *y, int64_t ldy, bool log_out) {
+                                                                   bool vec, U *y, int64_t ldy, bool log_out,
+                                                                   bool yvec) {
   extern __shared__ __align__(16) uint8_t srow_raw[];  // the row, when it fits
   T *srow = reinterpret_cast<T *>(srow_raw);
   __shared__ float red[2 * kRowThreads / 32];
+  constexpr int VT = 16 / sizeof(T);
   const bool cache = N * int64_t(sizeof(T)) <= kSmemRow;
   for (int64_t m = blockIdx.x; m < M; m += gridDim.x) {
     MaxSum acc{-INFINITY, 0.f};
@@ -196,7 +217,19 @@ __global__ void __launch_bounds__(kRowThreads) softmax_rows_kernel(const T *x, i
     const float inv = 1.f / r.s, lse = r.m + logf(r.s);
     U *yr = y + m * ldy;
     if (cache) {
-      for (int64_t i = threadIdx.x; i < N; i += kRowThreads) {
+      const int64_t nv = N / VT;  // shared memory rows are 16-byte aligned
+      for (int64_t i = threadIdx.x; i < nv; i += kRowThreads) {
+        const uint4 u = reinterpret_cast<const uint4 *>(srow)[i];
+        const T *e = reinterpret_cast<const T *>(&u);
+        float o[VT];
+#pragma unroll
+        for (int q = 0; q < VT; ++q) {
+          const float v = to_f<T>(e[q]);
+          o[q] = log_out ? v - lse : __expf(v - r.m) * inv;
+        }
+        store_outs<T, U>(yr + i * VT, o, yvec);
+      }
+      for (int64_t i = nv * VT + threadIdx.x; i < N; i += kRowThreads) {
         const float v = to_f<T>(srow[i]);
         yr[i] = from_f<U>(log_out ? v - lse : __expf(v - r.m) * inv);
       }
@@ -244,7 +277,7 @@ int row_grid(int64_t M) {
   int sms = 148;
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(M, int64_t(sms) * 8)));
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(M, int64_t(sms) * (2048 / kRowThreads))));
 }
 
 bool row_vec(const void *p, int64_t ld, int esz) {
@@ -321,6 +354,7 @@ int hx_softmax(const void *x, int dtype, int64_t M, int64_t N, int64_t ldx, void
   if (M < 0 || N <= 0 || ldx < N || ldy < N || (M > 0 && (!x || !y))) return HX_E_INVALID_ARG;
   if (M == 0) return HX_OK;
   const bool vec = hx::row_vec(x, ldx, hx::esz_of(dtype));
+  const bool yvec = hx::row_vec(y, ldy, hx::esz_of(y_dtype));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return hx::by_dtype(dtype, [&](auto tag) {
     using T = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
@@ -332,7 +366,7 @@ int hx_softmax(const void *x, int dtype, int64_t M, int64_t N, int64_t ldx, void
       cudaError_t e = hx::ensure_max_smem(kern, once, hx::kSmemRow);
       if (e != cudaSuccess) return hx::cuda_fail(e, "cudaFuncSetAttribute(softmax)");
       kern<<<hx::row_grid(M), hx::kRowThreads, smem, s>>>(static_cast<const T *>(x), M, N, ldx, vec,
-                                                          static_cast<U *>(y), ldy, log_softmax != 0);
+                                                          static_cast<U *>(y), ldy, log_softmax != 0, yvec);
       return hx::check_launch("softmax_rows_kernel");
     });
   });

@@ -306,7 +306,7 @@ int hx_conv2d(const hx_conv2d_desc *d, void *workspace, int64_t workspace_bytes,
 /* Softmax over rows of x[M, N] (dtype HX_F16 / HX_BF16 / HX_F32, row stride
    ldx), written to y (y_dtype, row stride ldy): y = exp(x - max) / sum, or the
    log-softmax x - max - log(sum) when log_softmax != 0.  One pass over x when
-   a row fits in shared memory (200 KB: N <= 102400 for 16-bit x), else two.  Reference: the row
+   a row fits in shared memory (112 KB: N <= 57344 for 16-bit x), else two.  Reference: the row
    softmax of test/python/triton/test_softmax.py and the online (running max,
    rescaled sum) softmax of test/python/triton/test_online_softmax.py. */
 int hx_softmax(const void *x, int dtype, int64_t M, int64_t N, int64_t ldx, void *y, int y_dtype,
