@@ -22,7 +22,14 @@
 // The mainloop and epilogue are those of gemm_sm100.cuh (TMA ring, tcgen05
 // UMMA into double-buffered TMEM, 8 epilogue warps), with the per-GEMM
 // parameters (tensor maps, sizes, instruction descriptor, SwiGLU, epilogue)
-// read from the launch's parameter block.
+// read from the launch's parameter block.  As there:
+//   * A and B come through 3-D tensor maps, KBS 128-byte K blocks per TMA
+//     instruction (TMA throughput here is per instruction, not per byte);
+//   * the weights (B) of a tile's first stages are requested before the
+//     producer waits for the tile's dependencies, so they are in flight
+//     while the producing GEMM finishes its row block;
+//   * full 32-column chunks leave through a per-warp staging buffer, so a
+//     store instruction writes whole 64 / 128-byte row segments.
 #pragma once
 #include <cuda.h>
 #include <stdint.h>
@@ -44,14 +51,15 @@ struct ChainGemm {
   int32_t tile_begin;  // first global tile number
   int32_t ctr_begin;   // first counter (one per row block)
   uint32_t idesc;      // UMMA instruction descriptor (f16 / bf16)
+  uint32_t idesc_half; // SWIGLU: the gate / up halves (N = BN / 2)
   EpiArgs epi;
 };
 
 struct ChainParams {
-  CUtensorMap tma[kChainMax];   // A operand maps
-  CUtensorMap tmb[kChainMax];   // B operand maps
+  CUtensorMap tma[kChainMax];   // A operand maps, 3-D {64 elements, rows, K blocks}
+  CUtensorMap tmb[kChainMax];   // B operand maps, same form
   ChainGemm g[kChainMax];
-  int32_t count, total_tiles, stages;
+  int32_t count, total_tiles, stages;  // stages of KBS K blocks each
   int32_t *counters;            // zeroed before launch
   int32_t *err_flag;
   uint64_t timeout;
@@ -86,19 +94,19 @@ __device__ __forceinline__ bool wait_counter(const int32_t *c, int target, uint6
   return true;
 }
 
-template <int BN>
+template <int BN, int KBS>
 __global__ void __launch_bounds__(kThreads, 1)
     hx_gemm_chain_kernel(const __grid_constant__ ChainParams p) {
-  constexpr int kABytes = kBM * kKBytes;
-  constexpr int kBBytes = BN * kKBytes;
-  constexpr int kStageBytes = kABytes + kBBytes;
-  constexpr int kBK = 64;  // 16-bit elements per 128-byte K block
+  constexpr int kABytes = kBM * kKBytes;           // one K block of A
+  constexpr int kBBytes = BN * kKBytes;            // one K block of B
+  constexpr int A_ST = KBS * kABytes, B_ST = KBS * kBBytes;
+  constexpr int kStageBytes = A_ST + B_ST;
   const int STAGES = p.stages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t *sA = smem;
-  uint8_t *sB = smem + STAGES * kABytes;
+  uint8_t *sB = smem + STAGES * A_ST;
   uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + STAGES * kStageBytes);
   uint64_t *empty_bar = full_bar + STAGES;
   uint64_t *tfull_bar = empty_bar + STAGES;
@@ -107,6 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *stored_bar = drain_bar + 1;  // [2] the 8 epilogue warps stored a tile
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(stored_bar + 2);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  uint8_t *stage_out = reinterpret_cast<uint8_t *>(full_bar) + kBarBytes;  // 8 x 4 KB
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -140,12 +149,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     int64_t issued = 0;
     bool ok = true;
+    auto advance = [&](int &st, uint32_t &ph) {
+      if (++st == STAGES) {
+        st = 0;
+        ph ^= 1;
+      }
+    };
     for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
       const int gi = chain_find(p, t);
       const ChainGemm &g = p.g[gi];
       const int local = t - g.tile_begin;
       const int m_blk = local / g.n_tiles, n_blk = local % g.n_tiles;
-      // dependencies: full row block m of the producers of A and residual
+      const int stage_blocks = (g.k_blocks + KBS - 1) / KBS;
+      auto load_b = [&](uint64_t *fb, int st, int sb) {
+        uint8_t *dstB = sB + st * B_ST;
+        if (g.swiglu) {
+          const int n0 = n_blk * (BN / 2);
+          tma_load_3d(dstB, &p.tmb[gi], fb, 0, n0, sb * KBS);
+          tma_load_3d(dstB + B_ST / 2, &p.tmb[gi], fb, 0, g.n_half + n0, sb * KBS);
+        } else {
+          tma_load_3d(dstB, &p.tmb[gi], fb, 0, n_blk * BN, sb * KBS);
+        }
+      };
+      // 1. weights of the first stages, before any dependency wait
+      const int pre = min(STAGES, stage_blocks);
+      const int st0 = stage;
+      for (int i = 0; i < pre && ok; ++i) {
+        bool w = (lane == 0) ? mbar_wait(&empty_bar[stage], phase ^ 1, p.timeout, abort_flag) : true;
+        w = __shfl_sync(0xffffffffu, w, 0);
+        if (!w) {
+          if (lane == 0) raise_abort(abort_flag, p.err_flag, 32);
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
+          load_b(&full_bar[stage], stage, i);
+        }
+        __syncwarp();
+        ++issued;
+        advance(stage, phase);
+      }
+      if (!ok) break;
+      // 2. dependencies: full row block m of the producers of A and residual
       if (lane == 0) {
         if (g.a_dep >= 0)
           ok = wait_counter(p.counters + p.g[g.a_dep].ctr_begin + m_blk, p.g[g.a_dep].n_tiles,
@@ -158,8 +204,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) raise_abort(abort_flag, p.err_flag, 31);
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      for (int kb = 0; kb < g.k_blocks; ++kb) {
+      if (!ok) {
+        // the armed stages still expect their A bytes: fill them so the
+        // drain below completes (A's rows are valid memory)
+        if (lane == 0)
+          for (int i = 0, st = st0; i < pre; ++i, st = (st + 1 == STAGES ? 0 : st + 1))
+            tma_load_3d(sA + st * A_ST, &p.tma[gi], &full_bar[st], 0, m_blk * kBM, i * KBS);
+        break;
+      }
+      // 3. activations of those stages
+      if (lane == 0)
+        for (int i = 0, st = st0; i < pre; ++i, st = (st + 1 == STAGES ? 0 : st + 1))
+          tma_load_3d(sA + st * A_ST, &p.tma[gi], &full_bar[st], 0, m_blk * kBM, i * KBS);
+      __syncwarp();
+      // 4. the remaining stages
+      for (int sb = pre; sb < stage_blocks; ++sb) {
         bool w = (lane == 0) ? mbar_wait(&empty_bar[stage], phase ^ 1, p.timeout, abort_flag) : true;
         w = __shfl_sync(0xffffffffu, w, 0);
         if (!w) {
@@ -170,23 +229,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           uint64_t *fb = &full_bar[stage];
           mbar_arrive_expect_tx(fb, kStageBytes);
-          const int kx = kb * kBK;
-          tma_load_2d(sA + stage * kABytes, &p.tma[gi], fb, kx, m_blk * kBM);
-          uint8_t *dstB = sB + stage * kBBytes;
-          if (g.swiglu) {
-            const int n0 = n_blk * (BN / 2);
-            tma_load_2d(dstB, &p.tmb[gi], fb, kx, n0);
-            tma_load_2d(dstB + (BN / 2) * kKBytes, &p.tmb[gi], fb, kx, g.n_half + n0);
-          } else {
-            tma_load_2d(dstB, &p.tmb[gi], fb, kx, n_blk * BN);
-          }
+          tma_load_3d(sA + stage * A_ST, &p.tma[gi], fb, 0, m_blk * kBM, sb * KBS);
+          load_b(fb, stage, sb);
         }
         __syncwarp();
         ++issued;
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1;
-        }
+        advance(stage, phase);
       }
     }
     if (!ok && lane == 0) {
@@ -204,6 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true, any = false;
     for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x, ++it) {
       const ChainGemm &g = p.g[chain_find(p, t)];
+      const int stage_blocks = (g.k_blocks + KBS - 1) / KBS;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       bool w = (lane == 0) ? mbar_wait(&tempty_bar[acc], acc_phase ^ 1, p.timeout, abort_flag) : true;
@@ -215,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * BN;
-      for (int kb = 0; kb < g.k_blocks; ++kb) {
+      for (int sb = 0; sb < stage_blocks; ++sb) {
         bool f = (lane == 0) ? mbar_wait(&full_bar[stage], phase, p.timeout, abort_flag) : true;
         f = __shfl_sync(0xffffffffu, f, 0);
         if (!f) {
@@ -225,13 +274,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t a_base = smem_u32(sA + stage * kABytes);
-          const uint32_t b_base = smem_u32(sB + stage * kBBytes);
+          const uint32_t a_base = smem_u32(sA + stage * A_ST);
+          const uint32_t b_base = smem_u32(sB + stage * B_ST);
+          const int nj = min(KBS, g.k_blocks - sb * KBS);  // K blocks past K are zero-filled anyway
+          for (int j = 0; j < nj; ++j) {
 #pragma unroll
-          for (int k = 0; k < kKBytes / kUmmaKBytes; ++k)
-            umma_f16(d_tmem, sdesc_kmajor_sw128(a_base + k * kUmmaKBytes),
-                     sdesc_kmajor_sw128(b_base + k * kUmmaKBytes), g.idesc,
-                     (kb > 0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < kKBytes / kUmmaKBytes; ++k) {
+              const uint64_t ad = sdesc_kmajor_sw128(a_base + j * kABytes + k * kUmmaKBytes);
+              const uint32_t accum = (sb > 0 || j > 0 || k > 0) ? 1u : 0u;
+              if (g.swiglu) {
+                const uint32_t hb = (BN / 2) * kKBytes;
+                const uint64_t gd = sdesc_kmajor_sw128(b_base + j * hb + k * kUmmaKBytes);
+                const uint64_t ud = sdesc_kmajor_sw128(b_base + B_ST / 2 + j * hb + k * kUmmaKBytes);
+                umma_f16(d_tmem, ad, gd, g.idesc_half, accum);
+                umma_f16(d_tmem + BN / 2, ad, ud, g.idesc_half, accum);
+              } else {
+                umma_f16(d_tmem, ad, sdesc_kmajor_sw128(b_base + j * kBBytes + k * kUmmaKBytes), g.idesc,
+                         accum);
+              }
+            }
+          }
           umma_commit(&empty_bar[stage]);
           any = true;
         }
@@ -254,6 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int row_in_tile = q * 32 + lane;
+    uint8_t *stg = stage_out + (warp - 2) * 4096;
     int it = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
       const int gi = chain_find(p, t);
@@ -286,7 +349,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int n0 = n_blk * out_w + c * 32;
         epi_transform32(g.epi, v, up, m, n0);
-        epi_store32(g.epi, v, r, false, m, n0);
+        if (g.epi.c_vec_ok && n0 + 32 <= g.epi.N)
+          epi_store32_staged_rt(g.epi, v, r, false, m - lane, n0, stg);
+        else
+          epi_store32(g.epi, v, r, false, m, n0);
       }
       tc_fence_before();
       // Stores of this thread, then visible to later TMA (async-proxy) reads.

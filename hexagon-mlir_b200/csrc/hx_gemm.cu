@@ -894,6 +894,7 @@ int gemm_chain_impl(const hx_gemm_desc *descs, const int32_t *a_dep, const int32
     return HX_E_NO_DEVICE;
   }
   constexpr int BN = 128;
+  constexpr int KBS = 2;  // K blocks per TMA instruction: 3 stages of 64 KB
   static ChainParams p;  // ~26 KB, passed by value at launch
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);
@@ -908,6 +909,7 @@ int gemm_chain_impl(const hx_gemm_desc *descs, const int32_t *a_dep, const int32
     if (d->epilogue == HX_EPI_DEQUANT_SCALE) return unsupported("chain epilogue");
     if (!aligned16(d->A) || !aligned16(d->B) || (d->lda * 2) % 16 || (d->ldb * 2) % 16)
       return unsupported("chain operands need 16-byte aligned rows");
+    if (d->K % 64) return unsupported("chain GEMMs need K a multiple of 64 (whole 128-byte K blocks)");
     for (const int32_t dep : {a_dep[g], r_dep[g]}) {
       if (dep < -1 || dep >= g) return arg_fail("dependencies must name earlier GEMMs");
       if (dep >= 0 && descs[dep].M != d->M) return arg_fail("a dependency must have the same M");
@@ -926,11 +928,13 @@ int gemm_chain_impl(const hx_gemm_desc *descs, const int32_t *a_dep, const int32
     c.tile_begin = static_cast<int32_t>(tiles);
     c.ctr_begin = static_cast<int32_t>(ctrs);
     c.idesc = make_idesc(d->a_dtype == HX_F16 ? 0 : 1, false, kBM, BN);
+    c.idesc_half = make_idesc(d->a_dtype == HX_F16 ? 0 : 1, false, kBM, BN / 2);
     c.epi = make_epi(d);
-    rc = make_tmap(&p.tma[g], d->A, d->a_dtype, d->K, d->M, d->lda, 64, kBM);
+    const uint64_t kblocks = static_cast<uint64_t>(d->K) / 64;
+    rc = make_tmap3(&p.tma[g], d->A, d->a_dtype, 64, d->M, kblocks, d->lda, kBM, KBS);
     if (rc != HX_OK) return rc;
-    rc = make_tmap(&p.tmb[g], d->B, d->b_dtype, d->K, sw ? 2 * d->N : d->N, d->ldb, 64,
-                   sw ? BN / 2 : BN);
+    rc = make_tmap3(&p.tmb[g], d->B, d->b_dtype, 64, sw ? 2 * d->N : d->N, kblocks, d->ldb,
+                    sw ? BN / 2 : BN, KBS);
     if (rc != HX_OK) return rc;
     tiles += static_cast<int64_t>(c.m_tiles) * c.n_tiles;
     ctrs += c.m_tiles;
@@ -942,14 +946,15 @@ int gemm_chain_impl(const hx_gemm_desc *descs, const int32_t *a_dep, const int32
   }
   p.count = count;
   p.total_tiles = static_cast<int32_t>(tiles);
-  p.stages = std::min(8, (kMaxDynSmem - 1280) / stage_bytes(BN));
+  const int fixed = 1024 + kBarBytes + kStageOutBytes;
+  p.stages = std::min(8, (kMaxDynSmem - fixed) / (KBS * stage_bytes(BN)));
   p.counters = counters;
   p.err_flag = error_flag;
   p.timeout = kDefaultTimeout;
   cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int32_t) * ctrs, s);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(chain counters)");
-  auto kern = hx_gemm_chain_kernel<BN>;
-  const int smem = p.stages * stage_bytes(BN) + 1024 + 256;
+  auto kern = hx_gemm_chain_kernel<BN, KBS>;
+  const int smem = p.stages * KBS * stage_bytes(BN) + fixed;
   static SmemAttrOnce attr_once;
   e = ensure_max_smem(kern, attr_once);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(chain)");

@@ -163,7 +163,7 @@ class ChainRecorder:
     def accepts(self, d, a, b, residual, b_layout, tile_n, stages, max_ctas, force_simt):
         if b_layout != "nk" or tile_n or stages or max_ctas or force_simt:
             return False
-        if a.dtype not in (torch.float16, torch.bfloat16) or d.K == 0 or d.M == 0 or d.N == 0:
+        if a.dtype not in (torch.float16, torch.bfloat16) or d.K == 0 or d.M == 0 or d.N == 0 or d.K % 64:
             return False
         if d.epilogue == _lib.HX_EPI_DEQUANT_SCALE:
             return False
