@@ -138,13 +138,68 @@ __device__ __forceinline__ void for_row(const T *row, int64_t N, bool vec, F &&f
   }
 }
 
+// Visit a row 16 bytes at a time: fv(first index, float v[VT]) for whole
+// vectors (four loads in flight per thread), fs(index, v) for a ragged tail
+// or an unaligned row.
+template <typename T, typename FV, typename FS>
+__device__ __forceinline__ void for_row_vec(const T *row, int64_t N, bool vec, FV &&fv, FS &&fs) {
+  constexpr int V = 16 / sizeof(T);
+  constexpr int U = 4;
+  if (!vec) {
+    for (int64_t k = threadIdx.x; k < N; k += kRowThreads) fs(k, to_f<T>(row[k]));
+    return;
+  }
+  const int64_t nv = N / V;
+  const uint4 *r4 = reinterpret_cast<const uint4 *>(row);
+  int64_t i = threadIdx.x;
+  for (; i + (U - 1) * kRowThreads < nv; i += U * kRowThreads) {
+    uint4 u[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j) u[j] = __ldcs(r4 + i + j * kRowThreads);
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const T *e = reinterpret_cast<const T *>(&u[j]);
+      float v[V];
+#pragma unroll
+      for (int q = 0; q < V; ++q) v[q] = to_f<T>(e[q]);
+      fv((i + j * kRowThreads) * V, u[j], v);
+    }
+  }
+  for (; i < nv; i += kRowThreads) {
+    const uint4 u = __ldcs(r4 + i);
+    const T *e = reinterpret_cast<const T *>(&u);
+    float v[V];
+#pragma unroll
+    for (int q = 0; q < V; ++q) v[q] = to_f<T>(e[q]);
+    fv(i * V, u, v);
+  }
+  for (int64_t k = nv * V + threadIdx.x; k < N; k += kRowThreads) fs(k, to_f<T>(row[k]));
+}
+
+// Fold V values into a running {max, sum}: one max over the vector, one
+// rescale of the sum, then V exponentials.
+template <int V>
+__device__ __forceinline__ MaxSum ms_add_vec(MaxSum a, const float (&v)[V]) {
+  float mx = v[0];
+#pragma unroll
+  for (int q = 1; q < V; ++q) mx = fmaxf(mx, v[q]);
+  if (mx == -INFINITY) return a;
+  const float m = fmaxf(a.m, mx);
+  float s = a.m == -INFINITY ? 0.f : a.s * __expf(a.m - m);
+#pragma unroll
+  for (int q = 0; q < V; ++q) s += __expf(v[q] - m);
+  return {m, s};
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kRowThreads) softmax_stats_kernel(const T *x, int64_t M, int64_t N,
                                                                     int64_t ldx, bool vec, float *stats) {
   __shared__ float red[2 * kRowThreads / 32];
   for (int64_t m = blockIdx.x; m < M; m += gridDim.x) {
     MaxSum acc{-INFINITY, 0.f};
-    for_row(x + m * ldx, N, vec, [&](int64_t, float v) { acc = ms_add(acc, v); });
+    for_row_vec(x + m * ldx, N, vec, [&](int64_t, const uint4 &, const float (&v)[16 / sizeof(T)]) {
+      acc = ms_add_vec(acc, v);
+    }, [&](int64_t, float v) { acc = ms_add(acc, v); });
     const MaxSum r = block_merge(acc, red);
     if (threadIdx.x == 0) {
       stats[2 * m] = r.m;
@@ -209,7 +264,10 @@ __global__ void __launch_bounds__(kRowThreads) softmax_rows_kernel(const T *x, i
   const bool cache = N * int64_t(sizeof(T)) <= kSmemRow;
   for (int64_t m = blockIdx.x; m < M; m += gridDim.x) {
     MaxSum acc{-INFINITY, 0.f};
-    for_row(x + m * ldx, N, vec, [&](int64_t i, float v) {
+    for_row_vec(x + m * ldx, N, vec, [&](int64_t i, const uint4 &u, const float (&v)[VT]) {
+      acc = ms_add_vec(acc, v);
+      if (cache) *reinterpret_cast<uint4 *>(srow + i) = u;  // the raw vector
+    }, [&](int64_t i, float v) {
       acc = ms_add(acc, v);
       if (cache) srow[i] = from_f<T>(v);  // exact: v came from a T
     });
