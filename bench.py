@@ -720,8 +720,10 @@ def run_kernel_bench(args, world, rank, dev, peaks, peak_src):
                     "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in pin_out)},
             "gpu_launches": launches * args.steps,
             "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": runit,
-                         "frac": round(achieved / peak, 4), "traffic": None, "kernel": kern,
-                         "algorithmic_bytes": nbytes,
+                         "frac": round(achieved / peak, 4),
+                         "traffic": read_traffic({"attn": "batched_gpt2_attention.txt", "conv": "conv_3x3_implicit.txt",
+                                                  "softmax": "softmax_lmhead_vocab.txt"}[wl]),
+                         "kernel": kern, "algorithmic_bytes": nbytes,
                          "peak_source": f"{peak_src} " + ("bf16_tflops (burst)" if bound == "tensor" else "hbm_gbs")},
             "clocks": clocks}
     if rank == 0:
