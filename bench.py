@@ -235,7 +235,7 @@ def run_hx(args):
         return run_lmhead(args, world, rank, dev, peaks, peak_src)
     if args.workload == "tinyllama":
         return run_tinyllama(args, world, rank, dev, peaks, peak_src)
-    if args.workload in ("attn", "conv", "softmax"):
+    if args.workload in ("attn", "conv", "softmax", "cube"):
         return run_kernel_bench(args, world, rank, dev, peaks, peak_src)
     W = build_gpt2(dev) if args.workload == "gpt2" else build_qwen(dev)
     cg = W["cg"]
@@ -615,7 +615,23 @@ def run_kernel_bench(args, world, rank, dev, peaks, peak_src):
 
     g = torch.Generator().manual_seed(1240)
     wl = args.workload
-    if wl == "attn":
+    if wl == "cube":  # C = A.B, 1024^3 fp16, B[K,N], fp32 accumulate
+        a_h = torch.randn(1024, 1024, generator=g).half()
+        b_h = torch.randn(1024, 1024, generator=g).half()
+        host_in = [a_h, b_h]
+        a, b = a_h.to(dev), b_h.to(dev)
+        c = torch.empty(1024, 1024, dtype=torch.float16, device=dev)
+
+        def step():
+            ops.matmul(a, b, out=c)
+
+        outs = [c]
+        work = 2.0 * 1024 ** 3
+        nbytes = 2.0 * 3 * 1024 * 1024
+        launches, bound, kern = 1, "tensor", "hx_gemm_sm100_kernel (B[K,N])"
+        cfg = {"workload": "fp16 1024^3 matmul (BASELINE config 1)", "M": 1024, "N": 1024, "K": 1024}
+        metric, unit = "GEMM TFLOP/s", "TFLOP/s"
+    elif wl == "attn":
         B, Hh, S, D = 8, 12, 1024, 64
         q_h = torch.randn(B, Hh, S, D, generator=g).half()
         k_h = torch.randn(B, Hh, S, D, generator=g).half()
@@ -695,7 +711,7 @@ def run_kernel_bench(args, world, rank, dev, peaks, peak_src):
         rate = (work / (ms / 1e3) / 1e12) if unit == "TFLOP/s" else nbytes / (ms / 1e3) / 1e9
     # e2e: inputs from pinned host memory, the step, outputs back to pinned host memory
     pin_in = [t.pin_memory() for t in host_in]
-    dev_in = {"attn": lambda: [q, k, v], "conv": lambda: [x], "softmax": lambda: [x]}[wl]()
+    dev_in = {"attn": lambda: [q, k, v], "conv": lambda: [x], "softmax": lambda: [x], "cube": lambda: [a, b]}[wl]()
     pin_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
     e2e_ms = []
     for _ in range(max(3, min(args.steps, 10))):
@@ -722,7 +738,7 @@ def run_kernel_bench(args, world, rank, dev, peaks, peak_src):
             "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": runit,
                          "frac": round(achieved / peak, 4),
                          "traffic": read_traffic({"attn": "batched_gpt2_attention.txt", "conv": "conv_3x3_implicit.txt",
-                                                  "softmax": "softmax_lmhead_vocab.txt"}[wl]),
+                                                  "softmax": "softmax_lmhead_vocab.txt"}.get(wl, "")),
                          "kernel": kern, "algorithmic_bytes": nbytes,
                          "peak_source": f"{peak_src} " + ("bf16_tflops (burst)" if bound == "tensor" else "hbm_gbs")},
             "clocks": clocks}
@@ -762,7 +778,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["hx", "reference"], default="hx")
-    ap.add_argument("--workload", choices=["gpt2", "qwen", "tinyllama", "lmhead", "attn", "conv", "softmax"],
+    ap.add_argument("--workload", choices=["gpt2", "qwen", "tinyllama", "lmhead", "attn", "conv", "softmax", "cube"],
                     default="lmhead")
     ap.add_argument("--batch", type=int, default=1, help="decode batch M for --workload tinyllama")
     ap.add_argument("--layers", type=int, default=22, help="decoder layers for --workload tinyllama")

@@ -165,7 +165,17 @@ def _softmax(budget_s):
                 config={"workload": "LM-head vocabulary softmax, bf16 in place"})
 
 
-_TABLE = {"attn": _attn, "conv": _conv, "softmax": _softmax, "gpt2": _gpt2, "qwen": _qwen, "tinyllama": _tinyllama, "lmhead": _lmhead,
+def _cube(budget_s):
+    g = torch.Generator().manual_seed(1240)
+    a = torch.randn(1024, 1024, generator=g).half()
+    b = torch.randn(1024, 1024, generator=g).half()
+    t = _timeit(lambda: torch.matmul(a, b), 5)
+    return dict(metric="GEMM TFLOP/s", unit="TFLOP/s", dtype="fp16", value=round(2.0 * 1024 ** 3 / t / 1e12, 4),
+                ms_per_step=round(t * 1e3, 3), sample="PyTorch-CPU fp16 torch.matmul 1024^3, median of 5",
+                config={"workload": "fp16 1024^3 matmul (BASELINE config 1)"})
+
+
+_TABLE = {"cube": _cube, "attn": _attn, "conv": _conv, "softmax": _softmax, "gpt2": _gpt2, "qwen": _qwen, "tinyllama": _tinyllama, "lmhead": _lmhead,
           "lmhead_int8": lambda b: _lmhead(b, int8=True)}
 
 
