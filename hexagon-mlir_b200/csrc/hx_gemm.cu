@@ -978,6 +978,9 @@ int gemv_grouped_tc_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32
     const hx_w8a16_proj &q = projs[g];
     if (q.K % 128 || q.ldw % 16 || q.ldx % 8 || !aligned16(q.x) || !aligned16(q.W)) return kNeedsNoSplit;
   }
+  int kbs = 4;  // K blocks per weight TMA load
+  if (const char *env = std::getenv("HX_GT_KBS")) kbs = std::atoi(env);
+  if (kbs != 1 && kbs != 2) kbs = 4;
   static GtParams p;  // ~30 KB: built on the host, passed by value at launch
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);
@@ -990,7 +993,7 @@ int gemv_grouped_tc_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32
   for (int g = 0; g < count; ++g) {
     const hx_w8a16_proj &q = projs[g];
     int rc = make_tmap3(&p.tmW[g], q.W, HX_S8, 128, static_cast<uint64_t>(q.N),
-                        static_cast<uint64_t>(q.K / 128), static_cast<uint64_t>(q.ldw), 128, kGtKbStage);
+                        static_cast<uint64_t>(q.K / 128), static_cast<uint64_t>(q.ldw), 128, kbs);
     if (rc != HX_OK) return rc;
     GtDesc &d = p.d[g];
     d.x = static_cast<const __half *>(q.x);
@@ -1018,10 +1021,24 @@ int gemv_grouped_tc_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32
     if (r != cudaSuccess) return r;
     return launch_pdl(kern, dim3(grid), dim3(kGtThreads), smem, s, p);
   };
-  static SmemAttrOnce conf16, conf32, conf64;
-  if (M <= 16) e = launch(hx_gemv_w8a16_grouped_tc_kernel<16>, GtCfg<16>::kSmemBytes, conf16);
-  else if (M <= 32) e = launch(hx_gemv_w8a16_grouped_tc_kernel<32>, GtCfg<32>::kSmemBytes, conf32);
-  else e = launch(hx_gemv_w8a16_grouped_tc_kernel<64>, GtCfg<64>::kSmemBytes, conf64);
+  int nacc = M <= 16 ? 4 : (M <= 32 ? 2 : 1);
+  if (const char *env = std::getenv("HX_GT_NACC")) nacc = std::atoi(env);
+  static SmemAttrOnce conf[3][3][3];
+  const int kv = kbs == 1 ? 0 : (kbs == 2 ? 1 : 2);
+  const int av = nacc == 1 ? 0 : (nacc == 2 ? 1 : 2);
+#define HX_GT_LAUNCH(MP, KB, NAC)                                                                 \
+  launch(hx_gemv_w8a16_grouped_tc_kernel<MP, KB, NAC>, GtCfg<MP, KB, NAC>::kSmemBytes,            \
+         conf[MP == 16 ? 0 : (MP == 32 ? 1 : 2)][kv][av])
+#define HX_GT_LAUNCH_K(MP, NAC) \
+  (kbs == 1 ? HX_GT_LAUNCH(MP, 1, NAC) : (kbs == 2 ? HX_GT_LAUNCH(MP, 2, NAC) : HX_GT_LAUNCH(MP, 4, NAC)))
+#define HX_GT_LAUNCH_A(MP) \
+  (nacc == 1 ? HX_GT_LAUNCH_K(MP, 1) : (nacc == 2 ? HX_GT_LAUNCH_K(MP, 2) : HX_GT_LAUNCH_K(MP, 4)))
+  if (M <= 16) e = HX_GT_LAUNCH_A(16);
+  else if (M <= 32) e = HX_GT_LAUNCH_A(32);
+  else e = nacc == 1 ? HX_GT_LAUNCH_K(64, 1) : HX_GT_LAUNCH_K(64, 2);
+#undef HX_GT_LAUNCH_A
+#undef HX_GT_LAUNCH_K
+#undef HX_GT_LAUNCH
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "hx_gemv_w8a16_grouped_tc_kernel");
   return HX_OK;
@@ -1851,3 +1868,4 @@ int hx_shards_to_rows(const void *src, void *dst, int world, int64_t M, int64_t 
 }
 
 }  // extern "C"
+
