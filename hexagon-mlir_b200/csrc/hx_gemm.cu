@@ -26,6 +26,7 @@
 #include "gemm_sm100.cuh"
 #include "gemv_grouped.cuh"
 #include "gemv_grouped_tc.cuh"
+#include "gemv_grouped_mma.cuh"
 #include "gemv_w8a16.cuh"
 #include "w8a16_sm100.cuh"
 #include "hx_gemm.h"
@@ -1044,6 +1045,80 @@ int gemv_grouped_tc_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32
   return HX_OK;
 }
 
+// Register-fragment MMA grouped launch (gemv_grouped_mma.cuh) for M <= 16
+// when every projection has K % 64 == 0 and 16-byte aligned rows.  Returns
+// kNeedsNoSplit (internal) when it does not apply.
+int gemv_grouped_mma_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32_t *counters,
+                          int32_t *error_flag, cudaStream_t s, int sms) {
+  if (M > 16) return kNeedsNoSplit;
+  if (const char *env = std::getenv("HX_GROUPED_CUDA_CORE"))
+    if (std::atoi(env) > 0) return kNeedsNoSplit;
+  if (const char *env = std::getenv("HX_GROUPED_PATH"))  // tuning switch: "tc" or "cc" skip this kernel
+    if (std::strcmp(env, "mma") != 0) return kNeedsNoSplit;
+  // two 16-byte pieces of a row per lane (128-byte row segments per lane
+  // quad) when every K allows it, else one
+  int pieces = 2;
+  for (int g = 0; g < count; ++g) {
+    const hx_w8a16_proj &q = projs[g];
+    if (q.K % 64 || q.ldw % 16 || q.ldx % 8 || !aligned16(q.x) || !aligned16(q.W)) return kNeedsNoSplit;
+    if (q.K % 128) pieces = 1;
+  }
+  if (const char *env = std::getenv("HX_GM_P"))  // tuning switch
+    if (std::atoi(env) == 1) pieces = 1;
+  static GroupParams p;  // built on the host, passed by value at launch
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  p.G = count;
+  p.M = static_cast<int32_t>(M);
+  p.counters = counters;
+  p.err_flag = error_flag;
+  p.timeout = kDefaultTimeout;
+  int64_t items = 0;
+  for (int g = 0; g < count; ++g) {
+    const hx_w8a16_proj &q = projs[g];
+    GroupDesc &d = p.d[g];
+    d.W = q.W;
+    d.scale = static_cast<const __half *>(q.scale);
+    d.bias = static_cast<const __half *>(q.bias);
+    d.x = static_cast<const __half *>(q.x);
+    d.y = static_cast<__half *>(q.y);
+    d.N = static_cast<int32_t>(q.N);
+    d.K = static_cast<int32_t>(q.K);
+    d.ldw = static_cast<int32_t>(q.ldw);
+    d.ldx = static_cast<int32_t>(q.ldx);
+    d.ldy = static_cast<int32_t>(q.ldy);
+    d.dep = q.dep;
+    d.item_begin = static_cast<int32_t>(items);
+    d.rows = kGmRows;
+    d.signal = 0;
+    d.x_in_slot = 0;
+    if (q.dep >= 0) p.d[q.dep].signal = 1;
+    items += (q.N + kGmRows - 1) / kGmRows;
+    if (items > INT32_MAX) return unsupported("too many items");
+  }
+  p.total_items = static_cast<int32_t>(items);
+  // counters[count - 1] doubles as the work ticket (no projection signals it)
+  cudaError_t e = cudaMemsetAsync(counters, 0, sizeof(int32_t) * count, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(counters)");
+  auto launch = [&](auto kern) -> cudaError_t {
+    // every CTA must be resident at once (dependent items spin on counters)
+    int per_sm = 0;
+    cudaError_t r = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGmWarps * 32, 0);
+    if (r != cudaSuccess) return r;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    const int grid = static_cast<int>(std::max<int64_t>(
+        1, std::min<int64_t>(static_cast<int64_t>(per_sm) * sms, (items + kGmWarps - 1) / kGmWarps)));
+    r = launch_pdl(kern, dim3(grid), dim3(kGmWarps * 32), 0, s, p);
+    return r == cudaSuccess ? cudaGetLastError() : r;
+  };
+  if (pieces == 2)
+    e = M <= 8 ? launch(hx_gemv_w8a16_grouped_mma_kernel<1, 2>) : launch(hx_gemv_w8a16_grouped_mma_kernel<2, 2>);
+  else
+    e = M <= 8 ? launch(hx_gemv_w8a16_grouped_mma_kernel<1, 1>) : launch(hx_gemv_w8a16_grouped_mma_kernel<2, 1>);
+  if (e != cudaSuccess) return cuda_fail(e, "hx_gemv_w8a16_grouped_mma_kernel");
+  return HX_OK;
+}
+
 int gemv_grouped_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32_t *counters,
                       int32_t *error_flag, cudaStream_t s) {
   if (M < 0 || count < 0) return arg_fail("negative size");
@@ -1066,6 +1141,8 @@ int gemv_grouped_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32_t 
       return unsupported("size");
     if (q.dep >= g || q.dep < -1) return arg_fail("dep must name an earlier projection or be -1");
   }
+  rc = gemv_grouped_mma_impl(M, count, projs, counters, error_flag, s, sms);
+  if (rc != kNeedsNoSplit) return rc;
   rc = gemv_grouped_tc_impl(M, count, projs, counters, error_flag, s, sms);
   if (rc != kNeedsNoSplit) return rc;
   if (M > 8) return unsupported("grouped W8A16 on CUDA cores takes M <= 8");

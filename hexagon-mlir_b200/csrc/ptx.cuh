@@ -124,15 +124,6 @@ __device__ __forceinline__ void bulk_load_1d(void *smem_dst, const void *gsrc, u
       "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
-// 2-D tiled bulk tensor store shared -> global (bulk-group completion).
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *smem_src,
-                                             int32_t x, int32_t y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-          reinterpret_cast<uint64_t>(map)),
-      "r"(smem_u32(smem_src)), "r"(x), "r"(y)
-      : "memory");
-}
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

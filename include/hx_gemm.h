@@ -193,14 +193,17 @@ typedef struct hx_w8a16_proj {
 } hx_w8a16_proj;
 
 /* Run up to 256 W8A16 projections (a decode step's linears) in one
-   persistent launch, M <= 64, K % 16 == 0, 16-byte aligned rows.  Weight rows
-   stream into shared memory ahead of use; dependent projections wait on
-   per-projection completion counters.  Lists of at most 156 projections whose
-   K are all multiples of 128 run on the tensor cores (int8 -> fp16 exact
-   conversion, tcgen05 UMMA, fp32 accumulation); other lists, which must then
-   have M <= 8, run on CUDA cores.  `counters` is caller-owned device
-   scratch of `count` int32, zeroed by this call (cudaMemsetAsync on the
-   stream).  Same per-projection arithmetic as hx_gemv_w8a16 (reference:
+   persistent launch, M <= 64, K % 16 == 0, 16-byte aligned rows.  Dependent
+   projections wait on per-projection completion counters.  Kernel choice
+   (every kernel converts int8 -> fp16 exactly and accumulates in fp32):
+   M <= 16 with every K a multiple of 64: register-fragment tensor-core MMAs
+   fed straight from 128-bit weight loads; else, lists of at most 156
+   projections whose K are all multiples of 128: tcgen05 UMMA with the
+   converted weights in TMEM; other lists, which must then have M <= 8, run
+   on CUDA cores.  `counters` is caller-owned device scratch of `count`
+   int32, zeroed by this call (cudaMemsetAsync on the stream); the first
+   kernel also uses the last entry, which no projection signals, as its work
+   ticket.  Same per-projection arithmetic as hx_gemv_w8a16 (reference:
    dequantise + matmul, LinalgToLLVMPass.cpp:203-209); the grouping itself
    has no reference counterpart. */
 int hx_gemv_w8a16_grouped(int64_t M, int count, const hx_w8a16_proj *projs,

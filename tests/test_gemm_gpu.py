@@ -363,18 +363,27 @@ GROUPED_TC_SHAPES = [(2048, 2048, -1, 0.0015), (256, 2048, -1, 0.02), (5632, 204
 GROUPED_MIXED_SHAPES = GROUPED_TC_SHAPES[:5] + [(100, 48, -1, 0.02)]  # K=48: CUDA-core kernel
 
 
-@pytest.mark.parametrize("path,M", [("tc", 1), ("tc", 3), ("tc", 8), ("tc", 16), ("tc", 17),
+@pytest.mark.parametrize("path,M", [("mma", 1), ("mma", 3), ("mma", 8), ("mma", 9), ("mma", 16),
+                                    ("mma_p1", 1), ("mma_p1", 16),
+                                    ("tc", 1), ("tc", 3), ("tc", 8), ("tc", 16), ("tc", 17),
                                     ("tc", 32), ("tc", 50), ("tc", 64),
                                     ("mixed", 1), ("mixed", 3), ("mixed", 8),
                                     ("cuda_core", 1), ("cuda_core", 8)])
 def test_w8a16_grouped_chain(cuda_device, monkeypatch, path, M):
     """A decode-layer-like list in one launch: independent projections plus a
     dependent chain (q -> o, gate -> down), checked against the oracle.
-    "tc": every K a multiple of 128, the tensor-core kernel; "mixed": one
-    K=48 projection sends the list to the CUDA-core kernel; "cuda_core":
-    the CUDA-core kernel forced through HX_GROUPED_CUDA_CORE."""
+    "mma": M <= 16 with every K a multiple of 64, the register-fragment MMA
+    kernel (the default there; "mma_p1" with 16-byte row pieces per lane);
+    "tc": the tcgen05 kernel (the default for M > 16, forced below that
+    through HX_GROUPED_PATH); "mixed": one K=48 projection sends the list to
+    the CUDA-core kernel; "cuda_core": that kernel forced through
+    HX_GROUPED_CUDA_CORE."""
     if path == "cuda_core":
         monkeypatch.setenv("HX_GROUPED_CUDA_CORE", "1")
+    elif path == "tc":
+        monkeypatch.setenv("HX_GROUPED_PATH", "tc")
+    elif path == "mma_p1":
+        monkeypatch.setenv("HX_GM_P", "1")
     q = hx()
     d = cuda_device
     g = torch.Generator().manual_seed(30 + M)
