@@ -364,6 +364,27 @@ def run_tinyllama(args, world, rank, dev, peaks, peak_src):
     ms = total / args.steps
     nbytes = WL.tinyllama_decode_bytes(M, layers=args.layers)
     gbs = nbytes / (ms / 1e3) / 1e9
+
+    # End to end through the public W8A16Group API: this step's activations
+    # from pinned host memory, the launch, and the last projection's output
+    # read back to the host.
+    x_host, xi_host = x.cpu().pin_memory(), xi.cpu().pin_memory()
+    y_host = torch.empty(ys[-1].shape, dtype=ys[-1].dtype).pin_memory()
+    e2e_ms = []
+    for _ in range(args.steps):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        x.copy_(x_host, non_blocking=True)
+        xi.copy_(xi_host, non_blocking=True)
+        grp.run()
+        y_host.copy_(ys[-1], non_blocking=True)
+        e.record(stream)
+        e.synchronize()
+        e2e_ms.append(s.elapsed_time(e))
+    e2e_total = max_over_ranks(sum(e2e_ms), world, dev)
+    e2e_gbs = nbytes / (e2e_total / args.steps / 1e3) / 1e9
+    kernel = ("hx_gemv_w8a16_grouped_mma_kernel" if M <= 16 else "hx_gemv_w8a16_grouped_tc_kernel")
     peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
     line = {"metric": "W8A16 decode HBM GB/s", "value": round(gbs * world, 1), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
@@ -371,9 +392,15 @@ def run_tinyllama(args, world, rank, dev, peaks, peak_src):
             "config": {"workload": f"tinyllama-1.1b decode linears W8A16 M={M} (BASELINE config 4)",
                        "layers": args.layers, "M": M, "bytes_per_step": nbytes, "l2": "flushed before every step",
                        "parallelism": f"replicas{world}"},
+            "e2e": {"value": round(e2e_gbs * world, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": x_host.numel() * 2 + xi_host.numel() * 2,
+                    "d2h_bytes_per_step": y_host.numel() * 2,
+                    "api": "ops.W8A16Group.run (pinned host activations in, last output out)"},
             "gpu_launches": args.steps,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(gbs / peak, 4), "traffic": None, "kernel": "hx_gemv_w8a16_grouped_kernel",
+                         "frac": round(gbs / peak, 4),
+                         "traffic": read_traffic("gemv_w8a16_decode.txt") if M <= 16 else None,
+                         "kernel": kernel,
                          "peak_source": f"{peak_src} hbm_gbs"},
             "clocks": clocks}
     if rank == 0:

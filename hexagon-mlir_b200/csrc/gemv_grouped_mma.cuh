@@ -1,7 +1,8 @@
 // gemv_grouped_mma.cuh — a decode step's W8A16 projections in one persistent
 // launch, weights converted in registers and multiplied on the tensor cores
 // through warp-level register-operand MMAs (mma.sync m16n8k16, fp32
-// accumulate).  Used for batches M <= 16.
+// accumulate).  Used for batches M <= 16 (wider batches measured slower than
+// the tcgen05 kernel: the warp-level MMA rate, not HBM, bounds them).
 //
 // Same contract as hx_gemv_w8a16_grouped_kernel (gemv_grouped.cuh): a list of
 // projections y_g[M, N_g] = x_g[M, K_g] . (W_g * scale_g)^T (+ bias_g), W int8
@@ -51,8 +52,6 @@
 namespace hx {
 
 constexpr int kGmWarps = 8;   // warps per CTA
-constexpr int kGmRB = 2;      // 16-row blocks per item
-constexpr int kGmRows = 16 * kGmRB;
 
 __device__ __forceinline__ uint4 ld_stream_u4(const void *p) {
   uint4 v;
@@ -76,13 +75,13 @@ __device__ __forceinline__ uint32_t u4_word(const uint4 &v, int j) {
   return j == 0 ? v.x : (j == 1 ? v.y : (j == 2 ? v.z : v.w));
 }
 
-// NB: batch blocks of 8 (M <= 8 NB).  Lane (g8 = lane / 4, q = lane % 4)
-// owns rows g8 and g8 + 8 of each 16-row block.  P: 16-byte pieces of a row
-// per lane per chunk (a chunk is 64 P of K).
-template <int NB, int P>
+// NB: batch blocks of 8 (M <= 8 NB).  RB: 16-row blocks per item; lane
+// (g8 = lane / 4, q = lane % 4) owns rows g8 and g8 + 8 of each block.
+// P: 16-byte pieces of a row per lane per chunk (a chunk is 64 P of K).
+template <int NB, int RB, int P>
 __global__ void __launch_bounds__(kGmWarps * 32, 2)
     hx_gemv_w8a16_grouped_mma_kernel(const __grid_constant__ GroupParams p) {
-  constexpr int RB = kGmRB;
+  constexpr int kGmRows = 16 * RB;
   constexpr int kSeg = 16 * P;                                   // row bytes per lane per chunk
   constexpr int kChunk = 4 * kSeg;                               // K per chunk
   constexpr int kDepth = 8 / (RB * P) < 2 ? 2 : 8 / (RB * P);    // chunks in flight per lane

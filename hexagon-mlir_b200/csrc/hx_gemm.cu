@@ -1050,11 +1050,13 @@ int gemv_grouped_tc_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32
 // kNeedsNoSplit (internal) when it does not apply.
 int gemv_grouped_mma_impl(int64_t M, int count, const hx_w8a16_proj *projs, int32_t *counters,
                           int32_t *error_flag, cudaStream_t s, int sms) {
+  // Wider batches: measured 1.0-1.9 TB/s here against 2.3-2.8 on tcgen05.
   if (M > 16) return kNeedsNoSplit;
   if (const char *env = std::getenv("HX_GROUPED_CUDA_CORE"))
     if (std::atoi(env) > 0) return kNeedsNoSplit;
   if (const char *env = std::getenv("HX_GROUPED_PATH"))  // tuning switch: "tc" or "cc" skip this kernel
     if (std::strcmp(env, "mma") != 0) return kNeedsNoSplit;
+  const int rows = 32;
   // two 16-byte pieces of a row per lane (128-byte row segments per lane
   // quad) when every K allows it, else one
   int pieces = 2;
@@ -1089,11 +1091,11 @@ int gemv_grouped_mma_impl(int64_t M, int count, const hx_w8a16_proj *projs, int3
     d.ldy = static_cast<int32_t>(q.ldy);
     d.dep = q.dep;
     d.item_begin = static_cast<int32_t>(items);
-    d.rows = kGmRows;
+    d.rows = rows;
     d.signal = 0;
     d.x_in_slot = 0;
     if (q.dep >= 0) p.d[q.dep].signal = 1;
-    items += (q.N + kGmRows - 1) / kGmRows;
+    items += (q.N + rows - 1) / rows;
     if (items > INT32_MAX) return unsupported("too many items");
   }
   p.total_items = static_cast<int32_t>(items);
@@ -1111,10 +1113,11 @@ int gemv_grouped_mma_impl(int64_t M, int count, const hx_w8a16_proj *projs, int3
     r = launch_pdl(kern, dim3(grid), dim3(kGmWarps * 32), 0, s, p);
     return r == cudaSuccess ? cudaGetLastError() : r;
   };
-  if (pieces == 2)
-    e = M <= 8 ? launch(hx_gemv_w8a16_grouped_mma_kernel<1, 2>) : launch(hx_gemv_w8a16_grouped_mma_kernel<2, 2>);
-  else
-    e = M <= 8 ? launch(hx_gemv_w8a16_grouped_mma_kernel<1, 1>) : launch(hx_gemv_w8a16_grouped_mma_kernel<2, 1>);
+#define HX_GM_LAUNCH(P_)                                        \
+  (M <= 8 ? launch(hx_gemv_w8a16_grouped_mma_kernel<1, 2, P_>) \
+          : launch(hx_gemv_w8a16_grouped_mma_kernel<2, 2, P_>))
+  e = pieces == 2 ? HX_GM_LAUNCH(2) : HX_GM_LAUNCH(1);
+#undef HX_GM_LAUNCH
   if (e != cudaSuccess) return cuda_fail(e, "hx_gemv_w8a16_grouped_mma_kernel");
   return HX_OK;
 }
