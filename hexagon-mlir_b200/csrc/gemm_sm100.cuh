@@ -159,6 +159,12 @@ __device__ __forceinline__ void raise_abort(volatile int *abort_flag, int32_t *e
   if (err != nullptr) atomicExch(err, code);
 }
 
+// A raw-accumulator argument for store paths that do not read it.
+__device__ __forceinline__ const uint32_t (&v_as_raw_unused())[32] {
+  static __device__ const uint32_t kNone[32] = {};
+  return kNone;
+}
+
 // Epilogue of one accumulator row (TMEM lane quarter row, every other
 // 32-column chunk from c0): TMEM -> registers -> fused epilogue -> global.
 // With 16-bit operands (e.pre16) the scale / bias / residual of each chunk
@@ -177,6 +183,36 @@ __device__ __forceinline__ void epi_row_t(const EpiArgs &e, uint32_t t_row, int 
                                           Pre16 &pf, uint8_t *stg) {
   constexpr bool kRaw = (KIND == 2) && (CT == HX_S32) && (EPI == HX_EPI_NONE);
   constexpr bool kPre = !(EPI == HX_EPI_NONE || EPI == HX_EPI_SWIGLU);  // operands to prefetch
+#ifndef HX_EPI_NO_TMEM_PIPE
+  if constexpr (!SWIGLU && !kRaw) {
+    // The next chunk's TMEM load is in flight while this chunk is finished
+    // and stored (tcgen05.wait::ld waits for every earlier load, so the next
+    // load is issued only after this chunk's registers are consumed).
+    uint32_t r[32];
+    if (c0 < BN_OUT / 32) tmem_ld_32x32b_x32(t_row + c0 * 32, r);
+#pragma unroll 1
+    for (int c = c0; c < BN_OUT / 32; c += 2) {
+      const int n0 = n_base + c * 32;
+      tmem_ld_wait();
+      float v[32], up[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if constexpr (KIND == 2)
+          v[j] = static_cast<float>(static_cast<int32_t>(r[j]));
+        else
+          v[j] = __uint_as_float(r[j]);
+        up[j] = 0.f;
+      }
+      if (c + 2 < BN_OUT / 32) tmem_ld_32x32b_x32(t_row + (c + 2) * 32, r);
+      epi_apply_t<EPI, CT>(e, v, up, m, pf, stg);
+      if constexpr (kPre) {
+        if (c + 2 < BN_OUT / 32) epi_prefetch_t<EPI>(e, m, n0 + 64, pf);
+      }
+      epi_store32_staged_t<CT, false>(e, v, v_as_raw_unused(), m - static_cast<int>(threadIdx.x & 31), n0, stg);
+    }
+  } else
+#endif
+  {
 #pragma unroll 1
   for (int c = c0; c < BN_OUT / 32; c += 2) {
     uint32_t r[32], r2[32];
@@ -204,6 +240,7 @@ __device__ __forceinline__ void epi_row_t(const EpiArgs &e, uint32_t t_row, int 
     }
     epi_store32_staged_t<CT, kRaw>(e, v, r, m - static_cast<int>(threadIdx.x & 31), n0, stg);
     if (threadIdx.x == 64 && c < 8) HX_GEMM_STAMP(9 + c);
+  }
   }
 }
 
