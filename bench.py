@@ -544,8 +544,13 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
     h2d = a_host.numel() * a_host.element_size()
     d2h = out_host.numel() * out_host.element_size()
 
-    peak_key = "bf16_tflops"
-    peak = float(peaks.get(peak_key, FALLBACK_PEAKS["bf16_tflops"])) * (2.0 if int8 else 1.0)
+    # A timed region long enough to run into the 1 kW power cap (seconds of
+    # back-to-back GEMMs) is measured against the sustained GEMM peak, a short
+    # one against the burst peak.
+    sustained = local_ms > 200.0 or "sw_power_cap" in (clocks or {}).get("reasons", [])
+    peak_key = "bf16_tflops_sustained" if sustained else "bf16_tflops"
+    burst = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])) * (2.0 if int8 else 1.0)
+    peak = float(peaks.get(peak_key, FALLBACK_PEAKS[peak_key])) * (2.0 if int8 else 1.0)
     unit = "TOP/s" if int8 else "TFLOP/s"
     dtname = "int8 (int32 acc)" if int8 else "bf16"
     my_flops = 2.0 * M * (n1 - n0) * K
@@ -560,7 +565,11 @@ def run_lmhead(args, world, rank, dev, peaks, peak_src):
         roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": unit,
                 "frac": round(achieved / peak, 4), "traffic": traffic,
                 "kernel": "hx_gemm_sm100_2sm_kernel", "per_launch_ms": round(per_launch, 5),
-                "peak_source": f"{peak_src} {peak_key} (burst)" + (" x2 (int8 dense rate)" if int8 else "")}
+                "frac_of_burst": round(achieved / burst, 4),
+                "peak_source": f"{peak_src} {peak_key} "
+                               + (f"(sustained: {local_ms:.0f} ms timed, clocks {clocks.get('reasons') if clocks else []})"
+                                  if sustained else "(burst)")
+                               + (" x2 (int8 dense rate)" if int8 else "")}
     else:
         # A fused compute+collective step: its target time is the slower of the
         # GEMM at the measured tensor peak and the bytes every rank must receive
