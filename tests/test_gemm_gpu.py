@@ -417,6 +417,39 @@ def test_w8a16_grouped_chain(cuda_device, monkeypatch, path, M):
         assert_close(to_np32(ys[i]), refs[-1])
 
 
+@pytest.mark.parametrize("path,M", [("mma", 1), ("mma", 8), ("mma", 13), ("mma_p1", 4),
+                                    ("tc", 1), ("tc", 24), ("cuda_core", 2)])
+def test_w8a16_grouped_bias_strided(cuda_device, monkeypatch, path, M):
+    """Bias, strided operands and a ragged last row block: x is a column slice
+    of a wider activation (ldx > K), the weight a column slice of a wider
+    int8 matrix (ldw > K), y a column slice of a wider output (ldy > N), and
+    N = 1000 leaves a partial last item; checked against the oracle."""
+    if path == "cuda_core":
+        monkeypatch.setenv("HX_GROUPED_CUDA_CORE", "1")
+    elif path == "tc":
+        monkeypatch.setenv("HX_GROUPED_PATH", "tc")
+    elif path == "mma_p1":
+        monkeypatch.setenv("HX_GM_P", "1")
+    q = hx()
+    d = cuda_device
+    g = torch.Generator().manual_seed(90 + M)
+    N, K = 1000, 1024
+    w_full = torch.randint(-127, 128, (N, K + 256), generator=g, dtype=torch.int64).to(torch.int8)
+    s = (torch.rand(N, generator=g) * 0.019 + 0.001).half()
+    b = (torch.randn(N, generator=g) * 0.1).half()
+    x_full = torch.randn(M, K + 128, generator=g).half()
+    w_dev, x_dev = w_full.to(d), x_full.to(d)
+    y_full = torch.full((M, N + 24), float("nan"), dtype=torch.float16, device=d)
+    grp = q.ops.W8A16Group(M, d)
+    grp.add(x_dev[:, 64:64 + K], w_dev[:, 128:128 + K], s.to(d), y_full[:, :N], bias=b.to(d))
+    grp.run()
+    torch.cuda.synchronize()
+    assert int(grp.error_flag.item()) == 0
+    ref = O.w8a16_ref(x_full[:, 64:64 + K].numpy(), w_full[:, 128:128 + K].numpy(), s.numpy(), b.numpy())
+    assert_close(to_np32(y_full[:, :N]), ref)
+    assert torch.isnan(y_full[:, N:]).all(), "stores past ldy's N columns"
+
+
 # ---------------------------------------------------------------- split-K (cluster DSMEM reduction)
 @pytest.mark.parametrize("split_k", [2, 3, 4, 8])
 @pytest.mark.parametrize("epilogue", ["none", "bias_residual", "bias_gelu_tanh", "swiglu"])
